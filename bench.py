@@ -1,0 +1,592 @@
+"""Benchmark harness (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2|cfg1|cfg3|cfg4|cfg5] [--m M]
+
+Workloads (synthetic seeded data, weights random-init):
+
+  cfg2 (default; configs[1])  LoRA delta -> merge -> per-channel int8 requantisation
+        at the Qwen3-0.6B layer shapes: 7 projections x r in {16, 128}, alpha = 2r
+        (scaling 2).  One step merges one decoder layer's 7 projections for both
+        adapters; successive steps walk 28 distinct layers (412 MB of fp16
+        weights), so every step reads weights that are not in L2.  Metric: delta
+        TFLOPS (2 r N K per projection); the kernel is HBM-bound, so the roofline
+        is reported in GB/s.  N GPUs: each rank merges its own layers (weak scaling,
+        no collective on the data path).
+  cfg1  W8A16 GEMM X[16,1024] x W[3072,1024]^T (the reference's CPU-runnable case),
+        rotating over 64 weight copies (> L2).  Metric GB/s.
+  cfg3  decode sweep over the Qwen3-0.6B linear stack: 28 layers x 7 projections
+        + LM head 1024->151936, M tokens (default 16).  Metric GB/s.
+  cfg4  prefill W8A16 at Llama-3-8B MLP shapes (4096->14336, 14336->4096), bf16,
+        M tokens (default 2048).  Metric TFLOPS.
+  cfg5  Llama-3-70B MLP W8A16 with 32 adapter int8 copies, column-parallel N-split
+        over the N GPUs with an NCCL all-gather of the output slices, M tokens
+        (default 16).  Metric GB/s (decode) or TFLOPS (M >= 512).
+
+Timing: W untimed warm-up steps, then exactly K steps between a barrier +
+synchronize on both sides, CUDA events on the launching stream, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+SRC = ROOT / "blackwell-inference-server_b200"
+for _p in (str(ROOT), str(SRC)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+QWEN = (("q_proj", 1024, 2048), ("k_proj", 1024, 1024), ("v_proj", 1024, 1024), ("o_proj", 2048, 1024),
+        ("gate_proj", 1024, 3072), ("up_proj", 1024, 3072), ("down_proj", 3072, 1024))
+LLAMA8B_MLP = ((4096, 14336), (14336, 4096))
+LLAMA70B_MLP = ((8192, 28672), (28672, 8192))
+QWEN_LAYERS = 28
+LM_HEAD = (1024, 151936)
+
+
+# ---------------------------------------------------------------------------
+# environment helpers
+# ---------------------------------------------------------------------------
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic(kernel: str, workload: str):
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(f"{kernel}@{workload}")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi sampler running only while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].strip().isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def randn(shape, std, dtype, gen, dev):
+    return (torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * std).to(dtype)
+
+
+class MergeRequantWorkload:
+    """cfg2: LoRA delta + merge + requant for one Qwen3-0.6B layer, r in {16, 128}, per step."""
+
+    name = "cfg2"
+    kernel = "lora_tc_kernel<requant>"
+    unit = "TFLOPS"
+    metric_kind = "tflops"
+    ranks_r = (16, 128)
+
+    def __init__(self, dev, rank, world, layers=QWEN_LAYERS):
+        from blackwell_ops import _lib
+
+        self.lib = _lib.lib
+        self.dev = dev
+        self.rank = rank
+        self.layers = layers
+        g = torch.Generator(device=dev).manual_seed(1000 + rank)
+        self.W, self.A, self.B, self.Q, self.S = [], [], [], [], []
+        for _ in range(layers):
+            self.W.append([randn((n, k), 0.02, torch.float16, g, dev) for _, k, n in QWEN])
+            self.A.append({r: [randn((r, k), 1.0 / math.sqrt(k), torch.float16, g, dev) for _, k, n in QWEN]
+                           for r in self.ranks_r})
+            self.B.append({r: [randn((n, r), 0.01, torch.float16, g, dev) for _, k, n in QWEN] for r in self.ranks_r})
+            self.Q.append({r: [torch.empty((n, k), dtype=torch.int8, device=dev) for _, k, n in QWEN]
+                           for r in self.ranks_r})
+            self.S.append({r: [torch.empty((n,), dtype=torch.float16, device=dev) for _, k, n in QWEN]
+                           for r in self.ranks_r})
+        self.flops = sum(2.0 * r * n * k for r in self.ranks_r for _, k, n in QWEN)
+        self.bytes = sum(2 * n * k + 2 * r * (n + k) + n * k + 2 * n for r in self.ranks_r for _, k, n in QWEN)
+        self.launches_per_step = len(self.ranks_r) * len(QWEN)
+
+    def config(self):
+        return workload_config("cfg2", 0)
+
+    def step(self, s, st, events=None):
+        li = (s + 7 * self.rank) % self.layers
+        for r in self.ranks_r:
+            for p, (_, k, n) in enumerate(QWEN):
+                if events is not None:
+                    events.append(torch.cuda.Event(enable_timing=True))
+                    events[-1].record()
+                rc = self.lib.bw_lora_merge_requant(
+                    self.W[li][p].data_ptr(), k, self.A[li][r][p].data_ptr(), self.B[li][r][p].data_ptr(), 2.0,
+                    self.Q[li][r][p].data_ptr(), k, self.S[li][r][p].data_ptr(), n, k, r, st)
+                if events is not None:
+                    events.append(torch.cuda.Event(enable_timing=True))
+                    events[-1].record()
+                if rc:
+                    raise RuntimeError(self.lib.bw_last_error().decode())
+
+    # -- end to end through the public API with host (pinned) buffers --
+    def e2e_setup(self):
+        g = torch.Generator().manual_seed(77 + self.rank)
+        self.hW = [(torch.randn((n, k), generator=g) * 0.02).half().pin_memory() for _, k, n in QWEN]
+        self.hA = {r: [(torch.randn((r, k), generator=g) / math.sqrt(k)).half().pin_memory() for _, k, n in QWEN]
+                   for r in self.ranks_r}
+        self.hB = {r: [(torch.randn((n, r), generator=g) * 0.01).half().pin_memory() for _, k, n in QWEN]
+                   for r in self.ranks_r}
+        self.hQ = {r: [torch.empty((n, k), dtype=torch.int8).pin_memory() for _, k, n in QWEN] for r in self.ranks_r}
+        self.hS = {r: [torch.empty((n,), dtype=torch.float16).pin_memory() for _, k, n in QWEN] for r in self.ranks_r}
+        self.h2d = sum(t.numel() * 2 for t in self.hW) + sum(
+            t.numel() * 2 for r in self.ranks_r for t in self.hA[r] + self.hB[r])
+        self.d2h = sum(n * k + 2 * n for _ in self.ranks_r for _, k, n in QWEN)
+
+    def e2e_step(self, s):
+        from blackwell_ops.cuda import lora_merge_requant
+
+        W = [t.to(self.dev, non_blocking=True) for t in self.hW]
+        for r in self.ranks_r:
+            for p in range(len(QWEN)):
+                A = self.hA[r][p].to(self.dev, non_blocking=True)
+                B = self.hB[r][p].to(self.dev, non_blocking=True)
+                q, sc = lora_merge_requant(W[p], A, B, 2.0)
+                self.hQ[r][p].copy_(q, non_blocking=True)
+                self.hS[r][p].copy_(sc, non_blocking=True)
+
+    # -- the reference's CPU PyTorch path on a bounded sample --
+    @staticmethod
+    def cpu_sample(step_index: int):
+        from oracle import torch_port
+
+        _, k, n = QWEN[step_index % len(QWEN)]
+        g = torch.Generator().manual_seed(step_index)
+        W = (torch.randn((n, k), generator=g) * 0.02).half()
+        flops = 0.0
+        t0 = time.perf_counter()
+        for r in MergeRequantWorkload.ranks_r:
+            A = (torch.randn((r, k), generator=g) / math.sqrt(k)).half()
+            B = (torch.randn((n, r), generator=g) * 0.01).half()
+            t0 = time.perf_counter() if r == MergeRequantWorkload.ranks_r[0] else t0
+            torch_port.merge_requant(W, A, B, 2.0)
+            flops += 2.0 * r * n * k
+        return flops, time.perf_counter() - t0, f"one projection ({n}x{k}) per step, r in {{16,128}}"
+
+
+class GemmSweepWorkload:
+    """cfg1 / cfg3 / cfg4: W8A16 GEMMs through bw_w8a16_gemm on resident weights."""
+
+    kernel = "w8a16_tc_kernel"
+
+    def __init__(self, name, dev, rank, world, m):
+        from blackwell_ops import _lib
+
+        self.lib = _lib.lib
+        self.dev = dev
+        self.name = name
+        self.m = m
+        g = torch.Generator(device=dev).manual_seed(2000 + rank)
+        if name == "cfg1":
+            shapes = [(1024, 3072)] * 64
+            self.xdtype = torch.float16
+            self.desc = "cfg1: W8A16 GEMM X[16,1024] x W[3072,1024]^T, fp16, rotating 64 weight copies (> L2)"
+        elif name == "cfg3":
+            shapes = [(k, n) for _ in range(QWEN_LAYERS) for _, k, n in QWEN] + [LM_HEAD]
+            self.xdtype = torch.float16
+            self.desc = f"cfg3: Qwen3-0.6B decode sweep, 28 layers x 7 projections + LM head, M={m}, fp16"
+        elif name == "cfg4":
+            shapes = list(LLAMA8B_MLP)
+            self.xdtype = torch.bfloat16
+            self.desc = f"cfg4: Llama-3-8B MLP prefill W8A16, M={m}, bf16"
+        else:
+            raise ValueError(name)
+        self.rot = name == "cfg1"
+        self.shapes = shapes
+        from blackwell_ops.kernels import quantize_weight_int8
+
+        self.Q, self.S, self.X, self.Y = [], [], [], []
+        for k, n in shapes:
+            w = randn((n, k), 0.02, self.xdtype, g, dev)
+            q, s = quantize_weight_int8(w)
+            del w
+            self.Q.append(q)
+            self.S.append(s)
+            self.X.append(randn((m, k), 1.0, self.xdtype, g, dev))
+            self.Y.append(torch.empty((m, n), dtype=self.xdtype, device=dev))
+        per = [n * k + 2 * n + 2 * m * k + 2 * m * n for k, n in shapes]
+        fl = [2.0 * m * n * k for k, n in shapes]
+        if self.rot:
+            self.bytes, self.flops = per[0], fl[0]
+            self.launches_per_step = 1
+        else:
+            self.bytes, self.flops = sum(per), sum(fl)
+            self.launches_per_step = len(shapes)
+        self.metric_kind = "tflops" if name == "cfg4" else "gbs"
+        self.unit = "TFLOPS" if name == "cfg4" else "GB/s"
+        ws = max(self.lib.bw_w8a16_gemm_workspace_size(m, n, k) for k, n in shapes)
+        self.ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.xcode = 1 if self.xdtype == torch.bfloat16 else 0
+
+    def config(self):
+        return workload_config(self.name, self.m)
+
+    def _gemm(self, i, st):
+        k, n = self.shapes[i]
+        rc = self.lib.bw_w8a16_gemm(self.X[i].data_ptr(), self.xcode, k, self.Q[i].data_ptr(), k, self.S[i].data_ptr(),
+                                    self.xcode, self.Y[i].data_ptr(), n, self.m, n, k, self.ws.data_ptr(),
+                                    self.ws.numel(), st)
+        if rc:
+            raise RuntimeError(self.lib.bw_last_error().decode())
+
+    def step(self, s, st, events=None):
+        idx = [s % len(self.shapes)] if self.rot else range(len(self.shapes))
+        for i in idx:
+            if events is not None:
+                events.append(torch.cuda.Event(enable_timing=True))
+                events[-1].record()
+            self._gemm(i, st)
+            if events is not None:
+                events.append(torch.cuda.Event(enable_timing=True))
+                events[-1].record()
+
+    def e2e_setup(self):
+        g = torch.Generator().manual_seed(5)
+        self.hX = [torch.randn(x.shape, generator=g).to(self.xdtype).pin_memory() for x in self.X]
+        self.hY = [torch.empty(y.shape, dtype=self.xdtype).pin_memory() for y in self.Y]
+        idx = [0] if self.rot else range(len(self.shapes))
+        self.h2d = sum(self.hX[i].numel() * 2 for i in idx)
+        self.d2h = sum(self.hY[i].numel() * 2 for i in idx)
+
+    def e2e_step(self, s):
+        from blackwell_ops.kernels import int8_gemm
+
+        idx = [s % len(self.shapes)] if self.rot else range(len(self.shapes))
+        for i in idx:
+            x = self.hX[i].to(self.dev, non_blocking=True)
+            self.hY[i].copy_(int8_gemm(x, self.Q[i], self.S[i]), non_blocking=True)
+
+    def cpu_sample(self, step_index: int):
+        from oracle import torch_port
+
+        i = step_index % len(self.shapes)
+        k, n = self.shapes[i]
+        if self.name == "cfg4":
+            n = min(n, 1024)  # bounded sample: a 1024-column slice of the projection
+        g = torch.Generator().manual_seed(step_index)
+        w = (torch.randn((n, k), generator=g) * 0.02).to(self.xdtype)
+        q, s = torch_port.quantize_weight_int8(w)
+        x = torch.randn((self.m, k), generator=g).to(self.xdtype)
+        t0 = time.perf_counter()
+        torch_port.int8_gemm(x, q, s)
+        dt = time.perf_counter() - t0
+        amount = (2.0 * self.m * n * k) if self.metric_kind == "tflops" else (n * k + 2 * n + 2 * self.m * (k + n))
+        return amount, dt, f"one projection per step ({n}x{k}, M={self.m})"
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+def make_workload(args, dev, rank, world):
+    if args.workload == "cfg2":
+        return MergeRequantWorkload(dev, rank, world)
+    if args.workload in ("cfg1", "cfg3", "cfg4"):
+        m = args.m if args.m else {"cfg1": 16, "cfg3": 16, "cfg4": 2048}[args.workload]
+        return GemmSweepWorkload(args.workload, dev, rank, world, m)
+    raise SystemExit(f"unknown workload {args.workload}")
+
+
+def amount_of(wl) -> float:
+    return wl.flops if wl.metric_kind == "tflops" else wl.bytes
+
+
+def scale_unit(amount: float, seconds: float, kind: str) -> float:
+    return amount / seconds / (1e12 if kind == "tflops" else 1e9)
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU PyTorch path (oracle port) on the host cores."""
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    if args.workload == "cfg2":
+        sample = MergeRequantWorkload.cpu_sample
+        kind, unit = "tflops", "TFLOPS"
+    else:
+        wl_cpu = GemmCpuShim(args)
+        sample, kind, unit = wl_cpu.cpu_sample, wl_cpu.metric_kind, wl_cpu.unit
+    for i in range(args.warmup):
+        sample(i)
+    tot, secs, desc = 0.0, 0.0, ""
+    for i in range(args.steps):
+        a, t, desc = sample(args.warmup + i)
+        tot += a
+        secs += t
+    v = scale_unit(tot, secs, kind)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 6), "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16" if args.workload != "cfg4" else "bf16",
+            "data": "synthetic (seeded), random-init weights",
+            "config": config_for(args),
+            "cpu_baseline": {"value": round(v, 6), "unit": unit, "cores": cores, "kind": "port", "sample": desc},
+            "e2e": {"value": round(v, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+class GemmCpuShim:
+    """CPU-only view of a GEMM workload's shapes for the reference arm (no GPU state)."""
+
+    def __init__(self, args):
+        self.name = args.workload
+        self.m = args.m if args.m else {"cfg1": 16, "cfg3": 16, "cfg4": 2048}.get(args.workload, 16)
+        self.xdtype = torch.bfloat16 if self.name == "cfg4" else torch.float16
+        if self.name == "cfg1":
+            self.shapes = [(1024, 3072)]
+        elif self.name == "cfg3":
+            self.shapes = [(k, n) for _, k, n in QWEN] + [LM_HEAD]
+        else:
+            self.shapes = list(LLAMA8B_MLP)
+        self.metric_kind = "tflops" if self.name == "cfg4" else "gbs"
+        self.unit = "TFLOPS" if self.name == "cfg4" else "GB/s"
+
+    cpu_sample = GemmSweepWorkload.cpu_sample
+
+
+METRIC = "W8A16 GEMM HBM GB/s (decode) / TFLOPS (prefill, ΔW) vs B200 roofline"
+
+DEFAULT_M = {"cfg1": 16, "cfg3": 16, "cfg4": 2048}
+
+
+def workload_config(name: str, m: int) -> dict:
+    """The `config` object of the JSON line; identical for both arms."""
+    if name == "cfg2":
+        return {"workload": "cfg2: LoRA delta+merge+requant, Qwen3-0.6B layer (7 projections), r in {16,128}, "
+                            "alpha=2r (scaling 2)", "layers_rotated": QWEN_LAYERS,
+                "l2": "inputs larger than L2: each step merges a different layer (28 layers, 412 MB fp16 W)",
+                "parallelism": "weak: each rank merges its own layers, no collective"}
+    m = m or DEFAULT_M[name]
+    desc = {"cfg1": "cfg1: W8A16 GEMM X[16,1024] x W[3072,1024]^T, fp16, 64 rotating weight copies",
+            "cfg3": f"cfg3: Qwen3-0.6B decode sweep, 28 layers x 7 projections + LM head, M={m}, fp16",
+            "cfg4": f"cfg4: Llama-3-8B MLP prefill W8A16 (4096->14336, 14336->4096), M={m}, bf16"}[name]
+    return {"workload": desc, "m": m, "l2": "inputs larger than L2 (weights streamed from HBM each step)",
+            "parallelism": "weak: independent replicas per rank"}
+
+
+def config_for(args, wl=None):
+    return wl.config() if wl is not None else workload_config(args.workload, args.m)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default="cfg2")
+    ap.add_argument("--m", type=int, default=0, help="tokens for the GEMM workloads")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    wl = make_workload(args, dev, rank, world)
+    st_ptr = torch.cuda.current_stream(dev).cuda_stream
+    peaks = load_peaks()
+
+    for s in range(args.warmup):
+        wl.step(s, st_ptr)
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- timed region ----
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(gpu_index(local))
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        start.record()
+        for s in range(args.steps):
+            wl.step(args.warmup + s, st_ptr)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms)
+
+    # ---- dominant-kernel duration, CUDA events around every launch ----
+    events: list = []
+    for s in range(args.steps):
+        wl.step(args.warmup + args.steps + s, st_ptr, events)
+    torch.cuda.synchronize()
+    kern_ms = sum(events[i].elapsed_time(events[i + 1]) for i in range(0, len(events), 2))
+    n_launch = len(events) // 2
+    kern_ms_per_step = kern_ms / args.steps
+
+    amount = amount_of(wl)
+    value = scale_unit(amount * world, ms_max / args.steps / 1e3, wl.metric_kind)
+    achieved_gbs = wl.bytes / (kern_ms_per_step / 1e3) / 1e9
+    achieved_tf = wl.flops / (kern_ms_per_step / 1e3) / 1e12
+    if wl.name == "cfg4" or (wl.name in ("cfg5",) and wl.metric_kind == "tflops"):
+        roof = {"bound": "tensor", "achieved": round(achieved_tf, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved_tf / peaks["bf16_tflops"], 4)}
+    else:
+        roof = {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved_gbs / peaks["hbm_gbs"], 4)}
+    roof["peak_source"] = peaks["source"] + " (MEASURED_PEAKS.json)" if peaks["source"] == "measured" else "fallback"
+    roof["traffic"] = load_traffic(wl.kernel, wl.name)
+    roof["kernel"] = wl.kernel
+    roof["launches_timed"] = n_launch
+    roof["bytes_per_step"] = wl.bytes
+    if wl.metric_kind == "tflops" and roof["bound"] == "hbm":
+        roof["tensor_tflops"] = round(achieved_tf, 2)
+
+    # ---- end to end through the public API, host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        wl.e2e_setup()
+        for s in range(args.warmup):
+            wl.e2e_step(s)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s in range(args.steps):
+            wl.e2e_step(s)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": round(scale_unit(amount * world, e_ms / args.steps / 1e3, wl.metric_kind), 4),
+               "unit": wl.unit, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
+               "ms_per_step": round(e_ms / args.steps, 4)}
+
+    from blackwell_ops import _lib
+
+    status = _lib.device_status(clear=False)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        torch.set_num_threads(os.cpu_count() or 1)
+        tot, secs, i, desc = 0.0, 0.0, 0, ""
+        while secs < 10.0 and i < 64:
+            a, t, desc = wl.cpu_sample(i)
+            if i > 0:  # first call warms the CPU path
+                tot += a
+                secs += t
+            i += 1
+        cpu = {"value": round(scale_unit(tot, secs, wl.metric_kind), 6), "unit": wl.unit,
+               "cores": torch.get_num_threads(), "kind": "port", "sample": desc + f", {i - 1} samples"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 4), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16" if getattr(wl, "xdtype", torch.float16) == torch.bfloat16 else "f16",
+                "data": "synthetic (seeded), random-init weights", "config": wl.config(), "roofline": roof,
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": wl.launches_per_step * args.steps,
+                "clocks": sampler.summary(), "device_status": status}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

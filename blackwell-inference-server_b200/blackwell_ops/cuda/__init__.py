@@ -1,0 +1,137 @@
+"""LoRA delta operators for B200 (drop-in for ``src/blackwell_ops/cuda/__init__.py``).
+
+Same names, arguments and error behaviour as the reference's CUDA extension
+for this path:
+
+* ``lora_delta(A, B, scaling)``        reference ``cuda/__init__.py:89`` -> ``lora_ops.cu:43-60``
+* ``lora_delta_tiled(A, B, scaling)``  reference ``cuda/__init__.py:99`` -> ``lora_tiled.cu:88-103``
+* ``add_delta_(W, delta)``             reference ``cuda/__init__.py:94`` -> ``lora_ops.cu:62-71``
+
+Both delta variants run the same tcgen05 kernel here (the reference's two
+kernels compute the same value).  Fused additions:
+
+* ``lora_merge(W, A, B, scaling, out=None)`` = ``add_delta_(W.clone(), lora_delta(A, B, scaling))``
+  without materialising the delta (``out=W`` merges in place).
+* ``lora_merge_requant(W, A, B, scaling)`` = ``quantize_weight_int8`` of that
+  merged weight, which is never written to memory.
+
+Errors are ``RuntimeError`` with the reference's TORCH_CHECK messages.
+Kernels run on torch's current stream (the reference used the legacy default
+stream).
+"""
+from __future__ import annotations
+
+import torch
+
+from .._lib import check, lib, stream_ptr
+
+
+def _check_ab(A: torch.Tensor, B: torch.Tensor) -> tuple[int, int, int]:
+    if not (A.is_cuda and B.is_cuda):
+        raise RuntimeError("A and B must be CUDA")
+    if A.dtype != torch.float16 or B.dtype != torch.float16:
+        raise RuntimeError("A and B must be fp16")
+    if A.dim() != 2 or B.dim() != 2:
+        raise RuntimeError("A and B must be 2D")
+    r, K = A.shape
+    N = B.shape[0]
+    if B.shape[1] != r:
+        raise RuntimeError("B must be [N, r]")
+    if A.device != B.device:
+        raise RuntimeError("A and B must be on the same device")
+    return r, K, N
+
+
+def lora_delta(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0) -> torch.Tensor:
+    """A: [r, K], B: [N, r] -> delta: [N, K] = B @ A * scaling (fp16, fp32 accumulation)"""
+    r, K, N = _check_ab(A, B)
+    A = A.contiguous()
+    B = B.contiguous()
+    delta = torch.empty((N, K), dtype=torch.float16, device=A.device)
+    if N and K:
+        if r == 0:
+            return delta.zero_()
+        with torch.cuda.device(A.device):
+            check(lib.bw_lora_delta(A.data_ptr(), B.data_ptr(), delta.data_ptr(), N, K, r, float(scaling),
+                                    stream_ptr(A.device)), "lora_delta")
+    return delta
+
+
+def lora_delta_tiled(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0) -> torch.Tensor:
+    """A: [r, K], B: [N, r] -> delta: [N, K] = B @ A * scaling (same kernel as lora_delta)"""
+    return lora_delta(A, B, scaling)
+
+
+def add_delta_(W: torch.Tensor, delta: torch.Tensor) -> None:
+    """W += delta, in-place (fp16(fp32 W + fp32 delta))."""
+    if not (W.is_cuda and delta.is_cuda):
+        raise RuntimeError("W and delta must be CUDA")
+    if W.dtype != torch.float16 or delta.dtype != torch.float16:
+        raise RuntimeError("must be fp16")
+    if W.numel() != delta.numel():
+        raise RuntimeError("shape mismatch")
+    if not W.is_contiguous():
+        raise RuntimeError("add_delta_: W must be contiguous")
+    delta = delta.contiguous()
+    if W.numel():
+        with torch.cuda.device(W.device):
+            check(lib.bw_add_delta(W.data_ptr(), delta.data_ptr(), W.numel(), stream_ptr(W.device)), "add_delta_")
+
+
+def _check_w(W: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    if not W.is_cuda:
+        raise RuntimeError("W must be CUDA")
+    if W.dtype != torch.float16:
+        raise RuntimeError("W must be fp16")
+    if W.dim() != 2 or tuple(W.shape) != (N, K):
+        raise RuntimeError(f"W must be [N, K] = [{N}, {K}]")
+    return W if W.stride(1) == 1 else W.contiguous()
+
+
+def lora_merge(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """W' = fp16(W + fp16(B @ A * scaling)); ``out=W`` merges in place."""
+    r, K, N = _check_ab(A, B)
+    W = _check_w(W, N, K)
+    A = A.contiguous()
+    B = B.contiguous()
+    if out is None:
+        out = torch.empty((N, K), dtype=torch.float16, device=W.device)
+    elif out.shape != W.shape or out.dtype != torch.float16 or out.stride(1) != 1:
+        raise RuntimeError("out must be an fp16 [N, K] tensor with unit column stride")
+    if N and K:
+        if r == 0:
+            if out.data_ptr() != W.data_ptr():
+                out.copy_(W)
+            return out
+        with torch.cuda.device(W.device):
+            check(lib.bw_lora_merge(W.data_ptr(), W.stride(0), A.data_ptr(), B.data_ptr(), float(scaling),
+                                    out.data_ptr(), out.stride(0), N, K, r, stream_ptr(W.device)), "lora_merge")
+    return out
+
+
+def lora_merge_requant(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
+                       scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """(w_int8, scale) = quantize_weight_int8(lora_merge(W, A, B, scaling)), fused."""
+    r, K, N = _check_ab(A, B)
+    W = _check_w(W, N, K)
+    if K == 0:
+        raise RuntimeError("lora_merge_requant: Expected reduction dim -1 to have non-zero size")
+    A = A.contiguous()
+    B = B.contiguous()
+    q = torch.empty((N, K), dtype=torch.int8, device=W.device)
+    scale = torch.empty((N,), dtype=torch.float16, device=W.device)
+    if N == 0:
+        return q, scale
+    if r == 0:
+        from ..kernels import quantize_weight_int8
+
+        return quantize_weight_int8(W)
+    with torch.cuda.device(W.device):
+        check(lib.bw_lora_merge_requant(W.data_ptr(), W.stride(0), A.data_ptr(), B.data_ptr(), float(scaling),
+                                        q.data_ptr(), K, scale.data_ptr(), N, K, r, stream_ptr(W.device)),
+              "lora_merge_requant")
+    return q, scale
+
+
+__all__ = ["lora_delta", "lora_delta_tiled", "add_delta_", "lora_merge", "lora_merge_requant"]

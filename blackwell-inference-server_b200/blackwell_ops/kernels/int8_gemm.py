@@ -1,0 +1,128 @@
+"""INT8 weight-only (W8A16) GEMM and per-channel int8 quantiser for B200.
+
+Drop-in for ``src/blackwell_ops/kernels/int8_gemm.py`` of the reference:
+
+* ``quantize_weight_int8(w)`` (reference ``:63-68``) -> ``(w_int8, scale)``,
+  bit-exact with the reference, computed by ``bw_quantize_rowwise_int8``.
+* ``int8_gemm(x, w_int8, scale)`` (reference ``:71-107``) -> ``y = x @ (w_int8 * scale).T``
+  in x.dtype with fp32 accumulation, computed by the tcgen05 kernel behind
+  ``bw_w8a16_gemm``.
+
+Both run on torch's current CUDA stream and allocate outputs with the caching
+allocator, as the reference does.  Split-K scratch is a per-(device, stream)
+workspace kept by this module; make one warm-up call before capturing a CUDA
+graph so the workspace exists.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from .._lib import DTYPE_CODE, check, lib, stream_ptr
+
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
+    """Per-(device, stream) split-K workspace; counters start (and stay) zero."""
+    if nbytes == 0:
+        return None
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+def reset_workspaces() -> None:
+    """Zero every cached workspace (needed only after a device-side timeout)."""
+    with _ws_lock:
+        for ws in _workspaces.values():
+            ws.zero_()
+
+
+def quantize_weight_int8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel symmetric int8 quantization.
+
+    ``w`` [..., K] fp16 / bf16 / fp32 on a CUDA device.  Returns ``w_int8``
+    (same shape, int8) and ``scale`` (``w.shape[:-1]``, w.dtype) with
+    ``scale = max|w_row| / 127`` (clamped >= 1e-8) and
+    ``w_int8 = clamp(round(w / scale), -127, 127)``, rounded exactly as the
+    reference rounds them.
+    """
+    if not w.is_cuda:
+        raise RuntimeError("quantize_weight_int8: w must be a CUDA tensor")
+    if w.dtype not in DTYPE_CODE:
+        raise RuntimeError(f"quantize_weight_int8: unsupported dtype {w.dtype}")
+    if w.dim() == 0:
+        raise RuntimeError("quantize_weight_int8: w must have at least one dimension")
+    k = w.shape[-1]
+    if k == 0:
+        raise RuntimeError("quantize_weight_int8: Expected reduction dim -1 to have non-zero size")
+    lead = tuple(w.shape[:-1])
+    w2 = w.reshape(-1, k)
+    if w2.stride(-1) != 1:
+        w2 = w2.contiguous()
+    n = w2.shape[0]
+    q = torch.empty((n, k), dtype=torch.int8, device=w.device)
+    scale = torch.empty((n,), dtype=w.dtype, device=w.device)
+    if n:
+        with torch.cuda.device(w.device):
+            check(
+                lib.bw_quantize_rowwise_int8(w2.data_ptr(), DTYPE_CODE[w.dtype], n, k, w2.stride(0), q.data_ptr(), k,
+                                             scale.data_ptr(), stream_ptr(w.device)),
+                "quantize_weight_int8",
+            )
+    return q.reshape(*lead, k), scale.reshape(lead)
+
+
+def int8_gemm(x: torch.Tensor, w_int8: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """
+    x: [M, K] fp16 / bf16
+    w_int8: [N, K] int8
+    scale: [N] fp16 / bf16 / fp32
+    returns: [M, N] in x.dtype
+    """
+    if not (x.is_cuda and w_int8.is_cuda and scale.is_cuda):
+        raise RuntimeError("int8_gemm: x, w_int8 and scale must be CUDA tensors")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError(f"int8_gemm: x must be fp16 or bf16, got {x.dtype}")
+    if w_int8.dtype != torch.int8:
+        raise RuntimeError(f"int8_gemm: w_int8 must be int8, got {w_int8.dtype}")
+    if scale.dtype not in DTYPE_CODE:
+        raise RuntimeError(f"int8_gemm: unsupported scale dtype {scale.dtype}")
+    if x.dim() != 2 or w_int8.dim() != 2:
+        raise RuntimeError("int8_gemm: x must be [M, K] and w_int8 [N, K]")
+    M, K = x.shape
+    N = w_int8.shape[0]
+    if w_int8.shape[1] != K:
+        raise RuntimeError(f"int8_gemm: K mismatch ({K} vs {w_int8.shape[1]})")
+    if scale.numel() != N:
+        raise RuntimeError(f"int8_gemm: scale must have N={N} elements")
+    y = torch.empty(M, N, device=x.device, dtype=x.dtype)
+    if M == 0 or N == 0:
+        return y
+    if K == 0:
+        return y.zero_()
+    if x.stride(1) != 1 or x.stride(0) < K:
+        x = x.contiguous()
+    if w_int8.stride(1) != 1 or w_int8.stride(0) < K:
+        w_int8 = w_int8.contiguous()
+    scale = scale.reshape(N)
+    if scale.stride(0) != 1:
+        scale = scale.contiguous()
+    with torch.cuda.device(x.device):
+        st = stream_ptr(x.device)
+        nbytes = lib.bw_w8a16_gemm_workspace_size(M, N, K)
+        ws = _workspace(x.device, st, nbytes)
+        check(
+            lib.bw_w8a16_gemm(x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0), w_int8.data_ptr(), w_int8.stride(0),
+                              scale.data_ptr(), DTYPE_CODE[scale.dtype], y.data_ptr(), N, M, N, K,
+                              ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, st),
+            "int8_gemm",
+        )
+    return y

@@ -1,0 +1,49 @@
+// Quantiser arithmetic shared by the quantise kernel and the fused LoRA
+// merge + requantise kernel, so both produce the reference's bits
+// (src/blackwell_ops/kernels/int8_gemm.py:63-68):
+//   amaxc = dt(max(fp32(amax), 1e-8f)); scale = dt(fp32(amaxc) / 127.0f)
+//   q     = clamp(rint(dt(fp32(w) / fp32(scale))), -127, 127); NaN -> 0
+// dt() rounds to the weight dtype (RNE); divisions are IEEE (__fdiv_rn).
+#pragma once
+
+#include "common.cuh"
+
+namespace bw {
+
+template <int DT>
+__device__ __forceinline__ float round_dt(float x) {
+  if constexpr (DT == BW_DTYPE_F16) return __half2float(__float2half_rn(x));
+  else if constexpr (DT == BW_DTYPE_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  else return x;
+}
+
+template <int DT>
+__device__ __forceinline__ float elem_at(const uint8_t* row, int64_t i) {
+  if constexpr (DT == BW_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(row)[i]);
+  else if constexpr (DT == BW_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[i]);
+  else return reinterpret_cast<const float*>(row)[i];
+}
+
+template <int DT>
+__device__ __forceinline__ void store_scale(void* scale, int64_t row, float s) {
+  if constexpr (DT == BW_DTYPE_F16) static_cast<__half*>(scale)[row] = __float2half_rn(s);
+  else if constexpr (DT == BW_DTYPE_BF16) static_cast<__nv_bfloat16*>(scale)[row] = __float2bfloat16_rn(s);
+  else static_cast<float*>(scale)[row] = s;
+}
+
+// scale from the row's absolute maximum (NaN-propagating like torch.amax)
+template <int DT>
+__device__ __forceinline__ float scale_from_amax(float amax, bool has_nan) {
+  if (has_nan) return __int_as_float(0x7fc00000);
+  const float amaxc = round_dt<DT>(fmaxf(amax, 1e-8f));
+  return round_dt<DT>(__fdiv_rn(amaxc, 127.0f));
+}
+
+template <int DT>
+__device__ __forceinline__ int8_t quant_one(float w, float s) {
+  const float x = round_dt<DT>(__fdiv_rn(w, s));
+  if (x != x) return 0;
+  return static_cast<int8_t>(fminf(fmaxf(rintf(x), -127.0f), 127.0f));
+}
+
+}  // namespace bw

@@ -1,0 +1,123 @@
+/*
+ * bw_ops.h — C ABI of the B200 (sm_100a) W8A16 / LoRA-delta operator library.
+ *
+ * Every entry point takes plain device pointers, element counts, row strides
+ * (in elements) and a CUDA stream (cudaStream_t passed as void*; NULL = the
+ * legacy default stream).  Nothing allocates device memory: outputs and
+ * workspaces are supplied by the caller.  Every function returns a status
+ * code (BW_OK == 0); bw_status_string() names it and bw_last_error() gives
+ * the calling thread's detail message for the last failure.
+ *
+ * Kernels run asynchronously on the given stream.  A kernel whose bounded
+ * internal wait expires records a device-side status instead of hanging;
+ * read it with bw_device_status().
+ *
+ * Library: libbw_ops.so (built for sm_100a only).
+ */
+#ifndef BW_OPS_H
+#define BW_OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define BW_DTYPE_F16 0
+#define BW_DTYPE_BF16 1
+#define BW_DTYPE_F32 2
+
+/* status codes */
+#define BW_OK 0
+#define BW_ERR_INVALID_ARGUMENT 1 /* bad pointer / shape / dtype / stride */
+#define BW_ERR_WORKSPACE 2        /* workspace missing or too small */
+#define BW_ERR_CUDA 3             /* a CUDA runtime call failed (launch, config) */
+#define BW_ERR_DEVICE_TIMEOUT 4   /* a kernel's bounded wait expired (device status) */
+#define BW_ERR_UNSUPPORTED 5      /* device is not sm_100 or feature unavailable */
+
+const char* bw_status_string(int status);
+/* Detail of the calling thread's last non-OK return (empty string if none). */
+const char* bw_last_error(void);
+/* Library version, major*10000 + minor*100 + patch. */
+int bw_version(void);
+
+/*
+ * Per-output-channel symmetric int8 quantisation.
+ * Replaces quantize_weight_int8, src/blackwell_ops/kernels/int8_gemm.py:63-68.
+ *   w      [n, k] row stride ldw, dtype w_dtype (F16 | BF16 | F32)
+ *   q      [n, k] int8, row stride ldq
+ *   scale  [n] in w_dtype
+ * scale = dt(max|w_row| clamped >= 1e-8, / 127); q = clamp(rne(dt(w/scale)), +-127).
+ * Bit-exact with the reference.  n == 0 is a no-op; k must be >= 1.
+ */
+int bw_quantize_rowwise_int8(const void* w, int w_dtype, int64_t n, int64_t k, int64_t ldw,
+                             int8_t* q, int64_t ldq, void* scale, void* stream);
+
+/*
+ * W8A16 GEMM: y[m, n] = dt( (sum_k x[m,k] * w[n,k]) * scale[n] ), fp32 accumulation.
+ * Replaces int8_gemm, src/blackwell_ops/kernels/int8_gemm.py:71-107 (kernel :15-60).
+ *   x      [m, k] x_dtype (F16 | BF16), row stride ldx
+ *   w      [n, k] int8, row stride ldw
+ *   scale  [n] scale_dtype (F16 | BF16 | F32)
+ *   y      [m, n] x_dtype, row stride ldy
+ *   workspace: device memory of bw_w8a16_gemm_workspace_size() bytes whose
+ *   first bw_w8a16_gemm_workspace_zeroed_bytes() bytes are zero before the
+ *   first call (split-K tile counters; every successful call leaves them zero).
+ * Calls that share a workspace must not overlap on the GPU.
+ */
+size_t bw_w8a16_gemm_workspace_size(int64_t m, int64_t n, int64_t k);
+size_t bw_w8a16_gemm_workspace_zeroed_bytes(int64_t m, int64_t n, int64_t k);
+int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                  const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n,
+                  int64_t k, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * LoRA delta: delta[n, k] = fp16( fp32(sum_j b[n,j] * a[j,k]) * scaling ).
+ * Replaces lora_delta (src/blackwell_ops/cuda/lora_ops.cu:43-60) and
+ * lora_delta_tiled (src/blackwell_ops/cuda/lora_tiled.cu:88-103).
+ *   a [r, k] fp16 contiguous, b [n, r] fp16 contiguous, delta [n, k] fp16 contiguous.
+ */
+int bw_lora_delta(const void* a, const void* b, void* delta, int64_t n, int64_t k, int64_t r,
+                  float scaling, void* stream);
+
+/*
+ * In-place merge w[i] = fp16(fp32(w[i]) + fp32(delta[i])), i < numel.
+ * Replaces add_delta_, src/blackwell_ops/cuda/lora_ops.cu:62-71 (kernel :32-38).
+ */
+int bw_add_delta(void* w, const void* delta, int64_t numel, void* stream);
+
+/*
+ * Fused delta + merge: w_out = add_delta(w, lora_delta(a, b, scaling)) without
+ * materialising delta.  w_out may alias w (in-place merge).  fp16.
+ *   w [n, k] row stride ldw; w_out [n, k] row stride ldo.
+ * Composes lora_ops.cu:16-27 and :32-38; no single reference counterpart.
+ */
+int bw_lora_merge(const void* w, int64_t ldw, const void* a, const void* b, float scaling,
+                  void* w_out, int64_t ldo, int64_t n, int64_t k, int64_t r, void* stream);
+
+/*
+ * Fused delta + merge + per-channel requantisation of the merged weight:
+ * (q, scale) = quantize_weight_int8(add_delta(w, lora_delta(a, b, scaling))).
+ * The merged fp16 weight is never written to memory and no scratch memory is
+ * used.  q [n, k] int8 row stride ldq; scale [n] fp16.
+ * Composes lora_ops.cu:16-38 and int8_gemm.py:63-68.
+ */
+int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, const void* b, float scaling,
+                          int8_t* q, int64_t ldq, void* scale, int64_t n, int64_t k, int64_t r,
+                          void* stream);
+
+/*
+ * Device-side status of the current device: BW_OK, or BW_ERR_DEVICE_TIMEOUT
+ * if a kernel's bounded wait expired since the last clear.  Synchronises
+ * `stream`.  If `detail` is non-NULL it receives the failing wait site id.
+ * clear != 0 resets the status to BW_OK.
+ */
+int bw_device_status(int clear, int* detail, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BW_OPS_H */

@@ -1,0 +1,155 @@
+"""GPU parity: tcgen05 LoRA delta / merge / fused requantisation vs the oracle.
+
+The oracle reproduces the reference kernels' fp32 accumulator exactly (j-ordered
+sums; see oracle/lora.py).  The tensor core sums the same exact products in a
+different order, so a delta may differ from the reference by one fp16 ulp when
+the fp32 sum lands next to a rounding boundary: the tests require every value
+within one ulp of the oracle and count the differing fraction.  Requantisation
+is checked bit-exactly as ``quantize_weight_int8(merged)`` of the merged weight
+that the same kernels produce, and against the oracle's codes with at most a
+handful of +-1 code differences traced to those 1-ulp deltas.
+"""
+import numpy as np
+import pytest
+
+from cases import LORA_CASES
+from oracle import inputs, lora, quant
+from oracle.numerics import F16
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+QWEN = inputs.QWEN3_06B_PROJ
+
+
+def dev16(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float16)).to(dev)
+
+
+def within_ulp(got, want, scale_like=None):
+    """|got - want| <= one fp16 ulp of max(|want|, |scale_like|).  For merged
+    weights scale_like is the delta: a one-ulp difference in the delta survives
+    the addition even when W and the delta cancel."""
+    got = np.asarray(got, np.float16).astype(np.float64)
+    w16 = np.asarray(want, np.float16)
+    mag = np.abs(w16).astype(np.float64)
+    if scale_like is not None:
+        mag = np.maximum(mag, np.abs(np.asarray(scale_like, np.float16)).astype(np.float64))
+    ulp = np.spacing(mag.astype(np.float16)).astype(np.float64)
+    diff = np.abs(got - w16.astype(np.float64))
+    assert (diff <= ulp).all(), diff.max()
+    return float((diff > 0).mean())
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from blackwell_ops import _lib, cuda
+    from blackwell_ops.kernels import quantize_weight_int8
+
+    yield cuda, quantize_weight_int8
+    assert _lib.device_status() == 0
+
+
+def make(seed, r, n, k):
+    return inputs.lora_a(seed, r, k), inputs.lora_b(seed + 1, n, r), inputs.weight(seed + 2, n, k, F16)
+
+
+CASES = [(c[1], c[2], c[3], c[4], c[5]) for c in LORA_CASES] + [
+    (400 + i, r, n, k, 2.0) for i, (r, (_, k, n)) in enumerate((r, p) for r in (16, 128) for p in QWEN)
+] + [(450, 8, 128, 64, 2.0), (451, 64, 130, 136, 1.0), (452, 32, 1, 128, 2.0), (453, 16, 257, 1000, 2.0),
+      (454, 12, 50, 100, 2.0), (455, 16, 33, 100, 0.75)]  # last two: CUDA-core fallback layouts
+
+
+@pytest.mark.parametrize("seed,r,n,k,s", CASES)
+def test_lora_delta(seed, r, n, k, s, cuda_dev, ops):
+    cuda, _ = ops
+    A, B, _ = make(seed, r, n, k)
+    want = lora.lora_delta(A, B, s)
+    for fn in (cuda.lora_delta, cuda.lora_delta_tiled):
+        got = fn(dev16(A, cuda_dev), dev16(B, cuda_dev), s).cpu().numpy()
+        assert within_ulp(got, want) < 0.01
+    # the reference test's tolerance (test_lora_ops.py:15)
+    ref32 = (B.astype(np.float32) @ A.astype(np.float32)) * s
+    assert np.abs(got.astype(np.float32) - ref32).max() < 0.02
+
+
+@pytest.mark.parametrize("seed,r,n,k,s", CASES)
+def test_lora_merge_and_requant(seed, r, n, k, s, cuda_dev, ops):
+    cuda, qz = ops
+    A, B, W = make(seed, r, n, k)
+    Ad, Bd, Wd = dev16(A, cuda_dev), dev16(B, cuda_dev), dev16(W, cuda_dev)
+    want = lora.merge(W, A, B, s)
+    merged = cuda.lora_merge(Wd, Ad, Bd, s)
+    assert within_ulp(merged.cpu().numpy(), want, lora.lora_delta(A, B, s)) < 0.01
+    # composition of the two reference ops gives the same bits as the fused merge
+    w2 = Wd.clone()
+    cuda.add_delta_(w2, cuda.lora_delta(Ad, Bd, s))
+    assert torch.equal(w2, merged)
+    # in-place merge
+    w3 = Wd.clone()
+    cuda.lora_merge(w3, Ad, Bd, s, out=w3)
+    assert torch.equal(w3, merged)
+    # fused requant == quantize(merged) exactly, and == the oracle's quantiser on that merged weight
+    q, sc = cuda.lora_merge_requant(Wd, Ad, Bd, s)
+    q2, sc2 = qz(merged)
+    assert torch.equal(q, q2) and torch.equal(sc, sc2)
+    qo, so = quant.quantize_weight_int8(merged.cpu().numpy(), F16)
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(sc.cpu().numpy(), so)
+    # against the oracle's own pipeline: codes differ only where a merged value differs by one ulp
+    qo2, _, _ = lora.merge_requant(W, A, B, s)
+    d = np.abs(q.cpu().numpy().astype(np.int32) - qo2.astype(np.int32))
+    assert d.max() <= 1
+    assert (d > 0).mean() < 1e-3
+
+
+def test_add_delta_bit_exact(cuda_dev, ops):
+    cuda, _ = ops
+    for n, k in ((64, 128), (3, 5), (1024, 1001)):
+        W = inputs.weight(11 + n, n, k, F16, std=1.0)
+        D = inputs.weight(12 + n, n, k, F16, std=1.0)
+        Wd = dev16(W, cuda_dev)
+        cuda.add_delta_(Wd, dev16(D, cuda_dev))
+        assert np.array_equal(Wd.cpu().numpy(), lora.add_delta(W, D))
+    # unaligned views take the scalar path
+    Wd = dev16(inputs.weight(1, 1, 1001, F16), cuda_dev)
+    Dd = dev16(inputs.weight(2, 1, 1001, F16), cuda_dev)
+    a, b = Wd[0, 1:], Dd[0, :1000]
+    want = lora.add_delta(a.cpu().numpy(), b.cpu().numpy())
+    cuda.add_delta_(a, b)
+    assert np.array_equal(a.cpu().numpy(), want)
+
+
+def test_lora_errors_match_reference_messages(cuda_dev, ops):
+    cuda, _ = ops
+    A = torch.randn(16, 128, device=cuda_dev, dtype=torch.float16)
+    B = torch.randn(96, 16, device=cuda_dev, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="A and B must be CUDA"):
+        cuda.lora_delta(A.cpu(), B)
+    with pytest.raises(RuntimeError, match="A and B must be fp16"):
+        cuda.lora_delta(A.float(), B)
+    with pytest.raises(RuntimeError, match="B must be"):
+        cuda.lora_delta(A, B[:, :8])
+    with pytest.raises(RuntimeError, match="shape mismatch"):
+        cuda.add_delta_(B.clone(), A)
+    with pytest.raises(RuntimeError, match="must be fp16"):
+        cuda.add_delta_(B.float(), B)
+
+
+def test_lora_full_size_70b_requant_properties(cuda_dev, ops):
+    """Llama-3-70B down-projection shard: K = 28672 (224 k-tiles, clusters of 8, two passes)."""
+    cuda, qz = ops
+    n, k, r = 1024, 28672, 64
+    g = torch.Generator(device=cuda_dev).manual_seed(9)
+    W = (torch.randn(n, k, generator=g, device=cuda_dev) * 0.02).half()
+    A = (torch.randn(r, k, generator=g, device=cuda_dev) / k ** 0.5).half()
+    B = (torch.randn(n, r, generator=g, device=cuda_dev) * 0.01).half()
+    merged = cuda.lora_merge(W, A, B, 2.0)
+    q, sc = cuda.lora_merge_requant(W, A, B, 2.0)
+    q2, sc2 = qz(merged)
+    assert torch.equal(q, q2) and torch.equal(sc, sc2)
+    d = 2.0 * (B.double() @ A.double())
+    ref = W.double() + d
+    err = (merged.double() - ref).abs()
+    # one fp16 rounding of the delta and one of the sum
+    assert bool((err <= (ref.abs() + d.abs()) * 2.0 ** -10 + 2.0 ** -24).all())
