@@ -27,16 +27,15 @@ def dev16(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float16)).to(dev)
 
 
-def within_ulp(got, want, scale_like=None):
-    """|got - want| <= one fp16 ulp of max(|want|, |scale_like|).  For merged
-    weights scale_like is the delta: a one-ulp difference in the delta survives
-    the addition even when W and the delta cancel."""
+def within_ulp(got, want, delta=None):
+    """|got - want| <= one fp16 ulp of want.  For merged weights add one ulp of
+    the delta: a delta that differs by one ulp changes the exact sum W + delta by
+    that much before the sum is rounded (at most one more ulp of the result)."""
     got = np.asarray(got, np.float16).astype(np.float64)
     w16 = np.asarray(want, np.float16)
-    mag = np.abs(w16).astype(np.float64)
-    if scale_like is not None:
-        mag = np.maximum(mag, np.abs(np.asarray(scale_like, np.float16)).astype(np.float64))
-    ulp = np.spacing(mag.astype(np.float16)).astype(np.float64)
+    ulp = np.spacing(np.abs(w16)).astype(np.float64)
+    if delta is not None:
+        ulp = ulp + np.spacing(np.abs(np.asarray(delta, np.float16))).astype(np.float64)
     diff = np.abs(got - w16.astype(np.float64))
     assert (diff <= ulp).all(), diff.max()
     return float((diff > 0).mean())
