@@ -68,6 +68,21 @@ struct GemmCfg {
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Named barrier that also ORs a predicate over the participating threads, so
+// every participant takes the same abort decision (a thread that left a loop
+// alone would otherwise leave its siblings waiting at a later bar.sync).
+__device__ __forceinline__ bool named_bar_any(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 template <bool BF16>
 __device__ __forceinline__ void convert_chunk(const uint4& v, uint4& o0, uint4& o1) {
@@ -231,7 +246,8 @@ __global__ void __launch_bounds__(192, 1)
     const int n = n0 + row;
     const bool ok = mbar_wait(tfull, 0, abort_flag, kSiteEpiTmem);
     tc_fence_after();
-    if (ok && !*abort_flag) {
+    const bool bad = named_bar_any(1, 128, !ok || *abort_flag);  // same decision in all 4 warps
+    if (!bad) {
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
       if (splits == 1) {
         const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
@@ -301,6 +317,365 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent variant for M <= 128 (decode and short prefill).
+//
+// One CTA per SM walks work units (n_tile, m_tile, k-split) with a stride of
+// gridDim.x; the TMA producer streams W/x stages continuously across units, so
+// the weight stream never drains between tiles.  448 threads:
+//   warp 0       TMA producer (STAGES-deep ring of [W int8 128x128 B | x BM x 128])
+//   warp 1       TMEM owner (512 columns) + tcgen05.mma issuer
+//   warps 2-9    dequantisers: thread = weight row, warps 2-5 take k columns
+//                0-63 and warps 6-9 columns 64-127 of a stage; int8 -> f16/bf16
+//                straight into a TMEM A buffer (tcgen05.st), 4 buffers x 64 cols
+//   warps 10-13  epilogue: double-buffered TMEM accumulators (2 x BM cols), so a
+//                unit's epilogue overlaps the next unit's mainloop
+// The MMA is the TS form: A (dequantised W) from TMEM, B (x) from shared memory.
+// Programmatic dependent launch: the producer waits (griddepcontrol.wait) only
+// before its first x load and the epilogue before its first global access, so
+// a dependent launch can stream weights while its predecessor finishes.
+// ---------------------------------------------------------------------------
+template <int BM>
+struct PCfg {
+  static constexpr int BK = 128;
+  static constexpr int W_BYTES = 128 * 128;
+  static constexpr int X_PANEL = BM * 128;
+  static constexpr int X_BYTES = 2 * X_PANEL;
+  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int ASTAGES = 4;  // TMEM A buffers, 64 columns each
+  static constexpr int A_COL0 = 0;
+  static constexpr int D_COL0 = ASTAGES * 64;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int OFF_W = 0;
+  static constexpr int OFF_X = STAGES * W_BYTES;
+  static constexpr int OFF_BAR = OFF_X + STAGES * X_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
+  static constexpr int THREADS = 448;
+  static_assert(BM >= 16 && BM <= 128 && BM % 16 == 0, "UMMA N for M=128");
+  static_assert(D_COL0 + 2 * BM <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert((2 * STAGES + 2 * ASTAGES + 4 + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
+};
+
+enum PersistentWaitSite : int {
+  kSitePProd = 111,
+  kSitePConvFull = 112,
+  kSitePConvA = 113,
+  kSitePMmaA = 114,
+  kSitePMmaFull = 115,
+  kSitePMmaD = 116,
+  kSitePEpi = 117,
+  kSitePDrain = 118,
+  kSitePFinal = 119,
+};
+
+template <int BM, bool BF16>
+__global__ void __launch_bounds__(448, 1)
+    w8a16_persistent_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                            const void* __restrict__ scale, int sdtype, void* __restrict__ y, int64_t ldy, int M,
+                            int N, int n_tiles, int kblocks, int kb_per_split, int splits, int units,
+                            float* __restrict__ ws, int* __restrict__ counters) {
+  using C = PCfg<BM>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int ASTAGES = C::ASTAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem + C::OFF_W;
+  uint8_t* sX = smem + C::OFF_X;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* afull = empty + STAGES;
+  uint64_t* aempty = afull + ASTAGES;
+  uint64_t* dfull = aempty + ASTAGES;    // 2
+  uint64_t* dempty = dfull + 2;          // 2
+  uint64_t* final_bar = dempty + 2;      // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* ticket = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8 + 1);  // 8 dequantiser warps + 1 MMA commit
+    }
+    for (int t = 0; t < ASTAGES; ++t) {
+      mbar_init(&afull[t], 8);
+      mbar_init(&aempty[t], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&dfull[b], 1);
+      mbar_init(&dempty[b], 4);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      // (unit, k-block) walk of this CTA
+      int u = blockIdx.x, i = 0;
+      auto unit_kb = [&](int uu, int& nt, int& mt, int& kb0, int& nkb) {
+        const int sp = uu % splits;
+        const int t = uu / splits;
+        nt = t % n_tiles;
+        mt = t / n_tiles;
+        kb0 = sp * kb_per_split;
+        nkb = min(kb_per_split, kblocks - kb0);
+      };
+      // Weights do not depend on the preceding kernel: fill the ring with weight
+      // tiles first, then wait for the predecessor (PDL) before loading x.
+      int pre = 0;
+      {
+        int uu = u, ii = 0;
+        while (uu < units && pre < STAGES) {
+          int nt, mt, kb0, nkb;
+          unit_kb(uu, nt, mt, kb0, nkb);
+          mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+          tma_load_2d(sW + pre * C::W_BYTES, &tm_w, &full[pre], (kb0 + ii) * C::BK, nt * 128, pol_w);
+          ++pre;
+          if (++ii == nkb) {
+            ii = 0;
+            uu += gridDim.x;
+          }
+        }
+      }
+      pdl_wait();
+      int it = 0;
+      bool ok = true;
+      while (u < units && ok) {
+        int nt, mt, kb0, nkb;
+        unit_kb(u, nt, mt, kb0, nkb);
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        const int kx = (kb0 + i) * C::BK;
+        if (it >= pre) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, kSitePProd)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], kx, nt * 128, pol_w);
+        }
+        tma_load_2d(sX + s * C::X_BYTES, &tm_x, &full[s], kx, mt * BM, pol_x);
+        tma_load_2d(sX + s * C::X_BYTES + C::X_PANEL, &tm_x, &full[s], kx + 64, mt * BM, pol_x);
+        ++it;
+        if (++i == nkb) {
+          i = 0;
+          u += gridDim.x;
+        }
+      }
+      if (!ok) {
+        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+          mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(128, BM, BF16, false);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
+        const int sp = u % splits;
+        const int kb0 = sp * kb_per_split;
+        const int nkb = min(kb_per_split, kblocks - kb0);
+        const int b = j & 1;
+        if (!mbar_wait(&dempty[b], ((j >> 1) & 1) ^ 1, abort_flag, kSitePMmaD)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + C::D_COL0 + b * BM;
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          const int t = it % ASTAGES;
+          const uint32_t pa = (it / ASTAGES) & 1;
+          if (!mbar_wait(&afull[t], pa, abort_flag, kSitePMmaA) || !mbar_wait(&full[s], ph, abort_flag, kSitePMmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t bd = make_sdesc(x_base + (kk >> 2) * C::X_PANEL + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+            umma_f16_ts(d_tmem, tmem + C::A_COL0 + t * 64 + kk * 8, bd, idesc, (i | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          umma_commit(&aempty[t]);
+        }
+        if (ok) umma_commit(&dfull[b]);
+      }
+      // every issued MMA has completed before TMEM is released
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, nullptr, kSitePFinal);
+    }
+  } else if (warp < 10) {
+    // ---------------- dequantisers ----------------
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const int sw = row & 7;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::A_COL0 + h * 32;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const int sp = u % splits;
+      const int kb0 = sp * kb_per_split;
+      const int nkb = min(kb_per_split, kblocks - kb0);
+      for (int i = 0; i < nkb; ++i, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        const int t = it % ASTAGES;
+        const uint32_t pa = (it / ASTAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, kSitePConvFull) ||
+            !mbar_wait(&aempty[t], pa ^ 1, abort_flag, kSitePConvA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* src = sW + s * C::W_BYTES + row * 128;
+        uint4 v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = *reinterpret_cast<const uint4*>(src + (((4 * h + c) ^ sw) << 4));
+        uint32_t out[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 o0, o1;
+          convert_chunk<BF16>(v[c], o0, o1);
+          out[8 * c + 0] = o0.x;
+          out[8 * c + 1] = o0.y;
+          out[8 * c + 2] = o0.z;
+          out[8 * c + 3] = o0.w;
+          out[8 * c + 4] = o1.x;
+          out[8 * c + 5] = o1.y;
+          out[8 * c + 6] = o1.z;
+          out[8 * c + 7] = o1.w;
+        }
+        tmem_st32(lane_base + t * 64, out);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&afull[t]);
+          mbar_arrive(&empty[s]);
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::D_COL0;
+    pdl_wait();
+    int j = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+      const int sp = u % splits;
+      const int t = u / splits;
+      const int nt = t % n_tiles;
+      const int mt = t / n_tiles;
+      const int n = nt * 128 + row;
+      const int m0 = mt * BM;
+      const int b = j & 1;
+      const bool ok = mbar_wait(&dfull[b], (j >> 1) & 1, abort_flag, kSitePEpi);
+      if (named_bar_any(1, 128, !ok || *abort_flag)) break;  // same decision in all 4 warps
+      tc_fence_after();
+      const uint32_t taddr = lane_addr + b * BM;
+      if (splits == 1) {
+        const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BM; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c0, r);
+          tmem_ld_wait();
+          if (n < N) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int m = m0 + c0 + e;
+              if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, __uint_as_float(r[e]) * sc);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dempty[b]);
+      } else {
+        float* mine = ws + (static_cast<size_t>(t) * splits + sp) * (128 * BM) + static_cast<size_t>(row) * BM;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BM; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(mine + c0 + e) = make_float4(
+                __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dempty[b]);  // accumulator free; partials are in global memory
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (warp == 10 && lane == 0) *ticket = atomicAdd(&counters[t], 1);
+        named_bar_sync(1, 128);
+        const bool last = *ticket == splits - 1;
+        named_bar_sync(1, 128);  // every thread has read the ticket before the next unit overwrites it
+        if (last) {
+          __threadfence();
+          const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
+          const float* base = ws + static_cast<size_t>(t) * splits * (128 * BM) + static_cast<size_t>(row) * BM;
+          for (int c0 = 0; c0 < BM; c0 += 4) {
+            float4 acc = __ldcg(reinterpret_cast<const float4*>(base + c0));
+            for (int p = 1; p < splits; ++p) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(base + static_cast<size_t>(p) * 128 * BM + c0));
+              acc.x += v.x;
+              acc.y += v.y;
+              acc.z += v.z;
+              acc.w += v.w;
+            }
+            if (n < N) {
+              const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int m = m0 + c0 + e;
+                if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, a4[e] * sc);
+              }
+            }
+          }
+          if (warp == 10 && lane == 0) counters[t] = 0;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // CUDA-core fallback for layouts TMA cannot address: one thread per output.
 template <bool BF16>
 __global__ void __launch_bounds__(128) w8a16_simt_kernel(const void* __restrict__ x, int64_t ldx,
@@ -322,30 +697,89 @@ __global__ void __launch_bounds__(128) w8a16_simt_kernel(const void* __restrict_
 // host planning
 // ---------------------------------------------------------------------------
 struct GemmPlan {
+  bool persistent = false;  // w8a16_persistent_kernel (M <= 128) or w8a16_tc_kernel
   int bm = 16;
-  int n_tiles = 0, m_tiles = 0, kblocks = 0, splits = 1, kb_per_split = 0;
+  int n_tiles = 0, m_tiles = 0, kblocks = 0, splits = 1, kb_per_split = 0, units = 0, grid = 0;
   size_t counter_bytes = 0, partial_bytes = 0;
 };
 
+// Persistent path: pick the split count that minimises the busiest CTA's work,
+// counting each k-block as 16 KB of weights and each unit a fixed overhead
+// (epilogue, pipeline hand-off) plus, when split, its fp32 partial round trip.
 static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k) {
   GemmPlan p;
-  p.bm = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
-  p.n_tiles = static_cast<int>((n + 127) / 128);
-  p.m_tiles = static_cast<int>((m + p.bm - 1) / p.bm);
-  p.kblocks = static_cast<int>((k + 127) / 128);
-  const int tiles = p.n_tiles * p.m_tiles;
   const int sms = num_sms();
-  int splits = 1;
-  if (tiles < sms) splits = sms / tiles;
-  if (splits > p.kblocks) splits = p.kblocks;
-  if (splits < 1) splits = 1;
-  p.kb_per_split = (p.kblocks + splits - 1) / splits;
-  p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.n_tiles = static_cast<int>((n + 127) / 128);
+  p.kblocks = static_cast<int>((k + 127) / 128);
+  if (m <= 128) {
+    p.persistent = true;
+    p.bm = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+    p.m_tiles = 1;
+    const int tiles = p.n_tiles;
+    double best = 1e300;
+    for (int sp = 1; sp <= p.kblocks && sp <= 32; ++sp) {
+      const int kbps = (p.kblocks + sp - 1) / sp;
+      const int real = (p.kblocks + kbps - 1) / kbps;
+      if (real != sp) continue;
+      const long units = static_cast<long>(tiles) * sp;
+      const long per_cta = (units + sms - 1) / sms;
+      const double unit_cost = kbps * 16384.0 + 6000.0 + (sp > 1 ? 2.0 * 128 * p.bm * 4 : 0.0);
+      const double cost = per_cta * unit_cost;
+      if (cost < best * 0.97) {
+        best = cost;
+        p.splits = sp;
+        p.kb_per_split = kbps;
+      }
+    }
+    p.units = tiles * p.splits;
+    p.grid = p.units < sms ? p.units : sms;
+  } else {
+    p.bm = 128;
+    p.m_tiles = static_cast<int>((m + p.bm - 1) / p.bm);
+    const int tiles = p.n_tiles * p.m_tiles;
+    int splits = tiles < sms ? sms / tiles : 1;
+    if (splits > p.kblocks) splits = p.kblocks;
+    if (splits < 1) splits = 1;
+    p.kb_per_split = (p.kblocks + splits - 1) / splits;
+    p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
+    p.units = tiles * p.splits;
+  }
   if (p.splits > 1) {
-    p.counter_bytes = ((static_cast<size_t>(tiles) * sizeof(int) + 255) / 256) * 256;
-    p.partial_bytes = static_cast<size_t>(tiles) * p.splits * 128 * p.bm * sizeof(float);
+    const size_t tiles = static_cast<size_t>(p.n_tiles) * p.m_tiles;
+    p.counter_bytes = ((tiles * sizeof(int) + 255) / 256) * 256;
+    p.partial_bytes = tiles * p.splits * 128 * p.bm * sizeof(float);
   }
   return p;
+}
+
+static bool g_use_pdl = true;
+
+template <int BM, bool BF16>
+static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale,
+                             int sdt, void* y, int64_t ldy, int M, int N, float* ws, int* counters, cudaStream_t st) {
+  using C = PCfg<BM>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(w8a16_persistent_kernel<BM, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::SMEM);
+  });
+  if (int s = check_cuda(attr_err, "cudaFuncSetAttribute(w8a16_persistent_kernel)")) return s;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_use_pdl ? 1 : 0;
+  return check_cuda(cudaLaunchKernelEx(&cfg, w8a16_persistent_kernel<BM, BF16>, tw, tx, scale, sdt, y, ldy, M, N,
+                                       p.n_tiles, p.kblocks, p.kb_per_split, p.splits, p.units, ws, counters),
+                    "cudaLaunchKernelEx(w8a16_persistent_kernel)");
 }
 
 template <int BM, bool BF16>
@@ -369,12 +803,15 @@ static int launch_tc(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
 template <bool BF16>
 static int dispatch_tc(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale, int sdt,
                        void* y, int64_t ldy, int M, int N, float* ws, int* counters, cudaStream_t st) {
-  switch (p.bm) {
-    case 16: return launch_tc<16, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-    case 32: return launch_tc<32, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-    case 64: return launch_tc<64, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-    default: return launch_tc<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+  if (p.persistent) {
+    switch (p.bm) {
+      case 16: return launch_persistent<16, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+      case 32: return launch_persistent<32, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+      case 64: return launch_persistent<64, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+      default: return launch_persistent<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+    }
   }
+  return launch_tc<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
 }
 
 static bool tma_ok(const void* p, int64_t ld_bytes) {
@@ -445,3 +882,4 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   if (bf16) return dispatch_tc<true>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
   return dispatch_tc<false>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
 }
+

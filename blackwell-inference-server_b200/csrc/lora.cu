@@ -118,7 +118,7 @@ __device__ __forceinline__ void lora_tile_epilogue(uint32_t taddr, uint8_t* sW, 
       } else {
         int8_t qv[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) qv[e] = quant_one<BW_DTYPE_F16>(wp[e], qscale);
+        for (int e = 0; e < 16; ++e) qv[e] = quant_fast<BW_DTYPE_F16>(wp[e], qscale, __frcp_rn(qscale));
         *reinterpret_cast<uint4*>(sQ + row * 128 + (((c0 >> 4) ^ sw) << 4)) = *reinterpret_cast<uint4*>(qv);
       }
     }
@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(128)
         for (int d = 0; d < cl_size; ++d) mbar_arrive_remote(mapa_shared(smem_u32(bar_x), d));
       }
       ok = mbar_wait_cluster(bar_x, 0, abort_flag, kSiteLoraXchg);
+      ok = !__syncthreads_or(!ok || *abort_flag);  // one decision for the whole CTA
       if (!ok) break;
       float m = 0.f;
       bool nn = false;
@@ -248,14 +249,14 @@ __global__ void __launch_bounds__(128)
       }
       ok = mbar_wait(bar_t, ph, abort_flag, kSiteLoraTile) && mbar_wait(bar_mma, ph, abort_flag, kSiteLoraMma);
       tc_fence_after();
-      if (ok && !*abort_flag) {
+      ok = !__syncthreads_or(!ok || *abort_flag);  // one decision for the whole CTA
+      if (ok) {
         if (MODE == kModeRequant && pass == 0) lora_tile_epilogue<MODE, 0>(taddr, sW, sQ, row, scaling, 0.f, pmax, nan);
         else lora_tile_epilogue<MODE, 1>(taddr, sW, sQ, row, scaling, qscale, pmax, nan);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncthreads();
-      ok = ok && !*abort_flag;
       if (tid == 0 && ok && !(MODE == kModeRequant && pass == 0)) {
         if (MODE == kModeRequant) {
           tma_store_2d(&tm_out, sQ, k0, n0);

@@ -46,4 +46,30 @@ __device__ __forceinline__ int8_t quant_one(float w, float s) {
   return static_cast<int8_t>(fminf(fmaxf(rintf(x), -127.0f), 127.0f));
 }
 
+// Same result as quant_one<DT>(w, s), faster.  With rcp = RN32(1/s),
+// x = RN32(w * rcp) lies within 2.5 fp32 ulps of RN32(w / s).  Rounding x to
+// dt (then to an integer) therefore gives the exact path's code unless x is
+// within 4 fp32 ulps of a dt rounding midpoint (fp16: low 13 mantissa bits
+// 0x1000; bf16: low 16 bits 0x8000), of an integer + 1/2 (fp32), or is not
+// finite.  Those lanes take the IEEE division.  Quotients below 1/2 in
+// magnitude give code 0 on both paths, so the fp16 subnormal range needs no
+// check.
+template <int DT>
+__device__ __forceinline__ int8_t quant_fast(float w, float s, float rcp) {
+  const float x = __fmul_rn(w, rcp);
+  const float ax = fabsf(x);
+  bool slow = !(ax < 1.0e30f);  // inf or NaN (zero scale, NaN input)
+  if constexpr (DT == BW_DTYPE_F16) {
+    const int d = static_cast<int>(__float_as_uint(x) & 0x1FFFu) - 0x1000;
+    slow |= (ax >= 0.5f) && (d >= -4 && d <= 4);
+  } else if constexpr (DT == BW_DTYPE_BF16) {
+    const int d = static_cast<int>(__float_as_uint(x) & 0xFFFFu) - 0x8000;
+    slow |= (ax >= 0.5f) && (d >= -4 && d <= 4);
+  } else {
+    slow |= fabsf(ax - floorf(ax) - 0.5f) <= 4.0e-5f;  // > 4 ulps for |x| < 256
+  }
+  if (slow) return quant_one<DT>(w, s);
+  return static_cast<int8_t>(fminf(fmaxf(rintf(round_dt<DT>(x)), -127.0f), 127.0f));
+}
+
 }  // namespace bw

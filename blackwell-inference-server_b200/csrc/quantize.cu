@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(512) quantize_rows_reg_kernel(const uint8_t* _
   }
   group_reduce(amax, nan, group, red, redn);
   const float s = scale_from_amax<DT>(amax, nan);
+  const float rcp = __frcp_rn(s);
   if (!active) return;
   if (g == 0) store_scale<DT>(scale, row, s);
 
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(512) quantize_rows_reg_kernel(const uint8_t* _
     chunk_values<DT>(v[i], f);
     int8_t out[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) out[e] = quant_one<DT>(f[e], s);
+    for (int e = 0; e < E; ++e) out[e] = quant_fast<DT>(f[e], s, rcp);
     if ((c + 1) * E <= k) {
       if constexpr (E == 8) {
         *reinterpret_cast<uint2*>(qr + c * E) = *reinterpret_cast<uint2*>(out);
@@ -166,8 +167,9 @@ __global__ void __launch_bounds__(256) quantize_rows_generic_kernel(const uint8_
   group_reduce(amax, nan, blockDim.x, red, redn);
   const float s = scale_from_amax<DT>(amax, nan);
   if (threadIdx.x == 0) store_scale<DT>(scale, row, s);
+  const float rcp = __frcp_rn(s);
   int8_t* qr = q + row * ldq;
-  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) qr[i] = quant_one<DT>(elem_at<DT>(wr, i), s);
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) qr[i] = quant_fast<DT>(elem_at<DT>(wr, i), s, rcp);
 }
 
 template <int DT, int VPT>

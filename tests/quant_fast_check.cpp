@@ -1,0 +1,122 @@
+// Exhaustive CPU check of the fast quantiser path used by the kernels
+// (csrc/quant_math.cuh: quant_fast vs quant_one).  Test infrastructure only.
+//
+// For every finite weight w and every positive finite scale s of the dtype,
+// the fast path (x = RN32(w * RN32(1/s)), exact division only when x is within
+// 4 fp32 ulps of a rounding midpoint, non-finite, or (fp32) near an integer +
+// 1/2) must give the same int8 code as the exact path
+// (clamp(rint(dt(RN32(w / s))), -127, 127), NaN -> 0).  x86-64 SSE float
+// arithmetic is IEEE single precision; build without fast-math or FP
+// contraction.
+//
+// usage: quant_fast_check f16|bf16|f32 [scale_stride]
+//   -> prints "mismatches=<n> slow=<n> total=<n>"; scale_stride > 1 checks every
+//   stride-th scale (all weights) to bound the run time.
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+static float bits_to_f(uint32_t b) { float f; std::memcpy(&f, &b, 4); return f; }
+static uint32_t f_to_bits(float f) { uint32_t b; std::memcpy(&b, &f, 4); return b; }
+
+static float f16_to_f(uint16_t h) { _Float16 v; std::memcpy(&v, &h, 2); return static_cast<float>(v); }
+static float round_f16(float x) { return static_cast<float>(static_cast<_Float16>(x)); }
+static float bf16_to_f(uint16_t h) { return bits_to_f(static_cast<uint32_t>(h) << 16); }
+static float round_bf16(float x) {
+  uint32_t u = f_to_bits(x);
+  if (std::isnan(x)) return x;
+  u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+  return bits_to_f(u);
+}
+
+enum { F16 = 0, BF16 = 1, F32 = 2 };
+
+template <int DT> static float round_dt(float x) {
+  if (DT == F16) return round_f16(x);
+  if (DT == BF16) return round_bf16(x);
+  return x;
+}
+
+template <int DT> static int8_t quant_exact(float w, float s) {
+  volatile float q = w / s;  // IEEE division
+  const float x = round_dt<DT>(q);
+  if (x != x) return 0;
+  return static_cast<int8_t>(std::fmin(std::fmax(std::rint(x), -127.0f), 127.0f));
+}
+
+template <int DT> static int8_t quant_fast(float w, float s, float rcp, long* slow_count) {
+  volatile float x = w * rcp;
+  const float ax = std::fabs(x);
+  bool slow = !(ax < 1.0e30f);
+  if (DT == F16) {
+    const int d = static_cast<int>(f_to_bits(x) & 0x1FFFu) - 0x1000;
+    slow |= (ax >= 0.5f) && (d >= -4 && d <= 4);
+  } else if (DT == BF16) {
+    const int d = static_cast<int>(f_to_bits(x) & 0xFFFFu) - 0x8000;
+    slow |= (ax >= 0.5f) && (d >= -4 && d <= 4);
+  } else {
+    slow |= std::fabs(ax - std::floor(ax) - 0.5f) <= 4.0e-5f;
+  }
+  if (slow) {
+    ++*slow_count;
+    return quant_exact<DT>(w, s);
+  }
+  return static_cast<int8_t>(std::fmin(std::fmax(std::rint(round_dt<DT>(x)), -127.0f), 127.0f));
+}
+
+template <int DT> static void run(int stride) {
+  // scales: every non-negative finite value of the dtype (fp32: a dense log sweep)
+  std::vector<float> scales, weights;
+  if (DT == F32) {
+    for (int e = -30; e <= 10; ++e)
+      for (int m = 0; m < 64; ++m) scales.push_back(std::ldexp(1.0f + m / 64.0f + 1.0f / 8192, e));
+    scales.push_back(0.0f);
+    for (uint32_t b = 0; b < 0x7F800000u; b += 99991) {  // ~21K magnitudes x 2 signs over all finite floats
+      weights.push_back(bits_to_f(b));
+      weights.push_back(-bits_to_f(b));
+    }
+  } else {
+    for (uint32_t h = 0; h < 0x7C00u + (DT == BF16 ? 0x0380u : 0u); ++h) {
+      const float v = DT == F16 ? f16_to_f(static_cast<uint16_t>(h)) : bf16_to_f(static_cast<uint16_t>(h));
+      if (std::isfinite(v)) scales.push_back(v);
+    }
+    for (uint32_t h = 0; h < 0x10000u; ++h) {
+      const float v = DT == F16 ? f16_to_f(static_cast<uint16_t>(h)) : bf16_to_f(static_cast<uint16_t>(h));
+      if (std::isfinite(v)) weights.push_back(v);
+    }
+  }
+  const int nt = std::max(1u, std::thread::hardware_concurrency());
+  std::vector<long> mism(nt, 0), slow(nt, 0), total(nt, 0);
+  std::vector<std::thread> th;
+  for (int t = 0; t < nt; ++t) {
+    th.emplace_back([&, t] {
+      for (size_t i = static_cast<size_t>(t) * stride; i < scales.size(); i += static_cast<size_t>(nt) * stride) {
+        const float s = scales[i];
+        volatile float one = 1.0f;
+        const float rcp = one / s;  // RN32(1/s)
+        for (float w : weights) {
+          if (quant_fast<DT>(w, s, rcp, &slow[t]) != quant_exact<DT>(w, s)) ++mism[t];
+          ++total[t];
+        }
+      }
+    });
+  }
+  for (auto& x : th) x.join();
+  long m = 0, sl = 0, tot = 0;
+  for (int t = 0; t < nt; ++t) { m += mism[t]; sl += slow[t]; tot += total[t]; }
+  std::printf("mismatches=%ld slow=%ld total=%ld\n", m, sl, tot);
+}
+
+int main(int argc, char** argv) {
+  if (argc < 2) return 2;
+  const int stride = argc > 2 ? std::atoi(argv[2]) : 1;
+  if (!std::strcmp(argv[1], "f16")) run<F16>(stride);
+  else if (!std::strcmp(argv[1], "bf16")) run<BF16>(stride);
+  else if (!std::strcmp(argv[1], "f32")) run<F32>(stride);
+  else return 2;
+  return 0;
+}

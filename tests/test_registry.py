@@ -47,15 +47,16 @@ def make_model(seed=0):
     return m.half()
 
 
-def make_adapter(model, r, seed, alpha=None):
+def make_adapter(n_layers, r, seed, alpha=None):
     g = torch.Generator().manual_seed(seed)
     alpha = alpha if alpha is not None else 2 * r
     out = {}
-    for name, mod in model.named_modules():
-        if isinstance(mod, torch.nn.Linear) and any(t in name for t in TARGETS):
-            A = (torch.randn(r, mod.in_features, generator=g) / mod.in_features ** 0.5).half()
-            B = (torch.randn(mod.out_features, r, generator=g) * 0.01).half()
-            out[name] = (A, B, alpha / r)
+    for i in range(n_layers):
+        for name in TARGETS:
+            k, n = SHAPES[name]
+            A = (torch.randn(r, k, generator=g) / k ** 0.5).half()
+            B = (torch.randn(n, r, generator=g) * 0.01).half()
+            out[f"layers.{i}.{name}"] = (A, B, alpha / r)
     return out
 
 
@@ -94,7 +95,7 @@ def test_registry_int8_copies_and_switching(cuda_dev):
     base_w = {n: m.weight.detach().clone() for n, m in model.named_modules() if isinstance(m, torch.nn.Linear)}
     reg = MultiDeltaLoRAModel(model, device="cuda")
     assert len(reg.layer_names) == 14
-    ad1, ad2 = make_adapter(model, 16, 1), make_adapter(model, 128, 2)
+    ad1, ad2 = make_adapter(2, 16, 1), make_adapter(2, 128, 2)
     assert reg.load_adapter("a", ad1) == 14
     assert reg.load_adapter("b", ad2) == 14
     x = torch.randn(3, 5, 256, device=cuda_dev).half()
@@ -126,8 +127,8 @@ def test_registry_fp16_mode_is_drift_free(cuda_dev):
 
     model = make_model(3)
     reg = MultiDeltaLoRAModel(model, device="cuda", quantize=False, targets=("q_proj", "v_proj"))
-    ad = make_adapter(model, 16, 5)
-    ad2 = make_adapter(model, 16, 6)
+    ad = make_adapter(2, 16, 5)
+    ad2 = make_adapter(2, 16, 6)
     reg.load_adapter("x", {k: v for k, v in ad.items() if "q_proj" in k or "v_proj" in k})
     reg.load_adapter("y", {k: v for k, v in ad2.items() if "q_proj" in k or "v_proj" in k})
     name = "layers.0.q_proj"
