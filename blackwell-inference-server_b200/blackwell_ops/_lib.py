@@ -37,6 +37,9 @@ SIGNATURES = {
     "bw_w8a16_gemm_workspace_zeroed_bytes": (_c.c_size_t, [_I64, _I64, _I64]),
     "bw_w8a16_gemm": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64, _P,
                                  _c.c_size_t, _P]),
+    "bw_w8a16_gemm_static_scratch_bytes": (_c.c_size_t, []),
+    "bw_w8a16_gemm_noalloc": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
+                                         _P]),
     "bw_lora_delta": (_c.c_int, [_P, _P, _P, _I64, _I64, _I64, _c.c_float, _P]),
     "bw_add_delta": (_c.c_int, [_P, _P, _I64, _P]),
     "bw_lora_merge": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),

@@ -883,3 +883,64 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   return dispatch_tc<false>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
 }
 
+// ---------------------------------------------------------------------------
+// GEMM entry point that allocates nothing (no counterpart in the reference).
+//
+// Some callers cannot give this library device memory: a serving runtime whose
+// memory manager reserves the whole GPU at start-up and refuses allocations
+// from plug-ins, or a foreign-language binding that has no handle on any CUDA
+// allocator.  For them the split-K scratch (tile counters + fp32 partials) is
+// this fixed array, one per GPU that loads the library, held until the process
+// exits.  Host code never uses the symbol directly: its device address is
+// looked up once per device with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------
+namespace bw {
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device (looked up on the
+// first call per device, with that device current).
+static int static_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (int s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return s;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev & 63] == nullptr) {
+    void* p = nullptr;
+    if (int s = check_cuda(cudaGetSymbolAddress(&p, g_static_scratch), "cudaGetSymbolAddress(static scratch)"))
+      return s;
+    addr[dev & 63] = p;
+  }
+  *out = addr[dev & 63];
+  return BW_OK;
+}
+}  // namespace bw
+
+extern "C" size_t bw_w8a16_gemm_static_scratch_bytes(void) { return bw::kStaticScratchBytes; }
+
+extern "C" int bw_w8a16_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                                     const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n,
+                                     int64_t k, void* stream) {
+  using namespace bw;
+  if (m > 0 && n > 0 && k > 0) {
+    const size_t need = bw_w8a16_gemm_workspace_size(m, n, k);
+    if (need > kStaticScratchBytes)
+      return fail(BW_ERR_WORKSPACE,
+                  "int8_gemm (no-alloc): m=%lld n=%lld k=%lld needs %zu bytes of split-K scratch, more than the "
+                  "%zu-byte static array",
+                  (long long)m, (long long)n, (long long)k, need, kStaticScratchBytes);
+    if (need > 0) {
+      void* scratch = nullptr;
+      if (int s = static_scratch_address(&scratch)) return s;
+      // the array keeps the previous call's contents: the tile counters must start at zero
+      const size_t zeroed = bw_w8a16_gemm_workspace_zeroed_bytes(m, n, k);
+      if (int s = check_cuda(cudaMemsetAsync(scratch, 0, zeroed, static_cast<cudaStream_t>(stream)),
+                             "clear static scratch counters"))
+        return s;
+      return bw_w8a16_gemm(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y, ldy, m, n, k, scratch,
+                           kStaticScratchBytes, stream);
+    }
+  }
+  return bw_w8a16_gemm(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y, ldy, m, n, k, nullptr, 0, stream);
+}

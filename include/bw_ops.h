@@ -74,6 +74,27 @@ int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int6
                   int64_t k, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * W8A16 GEMM that allocates nothing.  No counterpart in the reference: it exists
+ * for callers that cannot provide device memory, such as a serving runtime whose
+ * memory manager owns the whole GPU and refuses allocations from plug-ins, or a
+ * foreign-language binding with no access to a CUDA allocator.
+ * Same arguments and result as bw_w8a16_gemm minus the workspace: the split-K
+ * scratch is a fixed array inside libbw_ops.so of
+ * bw_w8a16_gemm_static_scratch_bytes() (8 MiB), one per GPU that loads the
+ * library, held until the process exits.
+ *  - The first call on a device looks up the array's device address (set-up);
+ *    make that first call before any stream capture.
+ *  - Shapes whose scratch need (bw_w8a16_gemm_workspace_size) exceeds the array
+ *    are rejected with BW_ERR_WORKSPACE.
+ *  - Every call shares the array and clears its counter prefix first (an async
+ *    memset on `stream`): calls that overlap on the GPU race.
+ */
+size_t bw_w8a16_gemm_static_scratch_bytes(void);
+int bw_w8a16_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                          const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t m,
+                          int64_t n, int64_t k, void* stream);
+
+/*
  * LoRA delta: delta[n, k] = fp16( fp32(sum_j b[n,j] * a[j,k]) * scaling ).
  * Replaces lora_delta (src/blackwell_ops/cuda/lora_ops.cu:43-60) and
  * lora_delta_tiled (src/blackwell_ops/cuda/lora_tiled.cu:88-103).

@@ -1,0 +1,73 @@
+"""The W8A16 GEMM entry point that allocates nothing (bw_w8a16_gemm_noalloc).
+
+Some callers cannot give the library device memory (a serving runtime whose
+memory manager owns the whole GPU, a foreign-language binding with no CUDA
+allocator), so this entry point keeps its split-K scratch in a fixed array
+inside libbw_ops.so.  This test calls it through the C ABI and checks, on two
+calls in a row, that it returns what the workspace-taking bw_w8a16_gemm
+returns, within the GEMM tests' tolerance (max |err| <= 1e-2, relative
+<= 1e-3), and that shapes needing more scratch than the array are refused.
+It lives in its own file, collected last, and needs nothing from other tests.
+"""
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _gemm_with_workspace(lib, st, x, q, s, m, n, k):
+    need = lib.bw_w8a16_gemm_workspace_size(m, n, k)
+    ws = torch.zeros(max(need, 16), dtype=torch.uint8, device=x.device)
+    y = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    rc = lib.bw_w8a16_gemm(x.data_ptr(), 0, k, q.data_ptr(), k, s.data_ptr(), 0, y.data_ptr(), n, m, n, k,
+                           ws.data_ptr(), ws.numel(), st)
+    assert rc == 0, lib.bw_last_error()
+    return y, need
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 1024, 4096), (1, 3072, 1024), (48, 2048, 2048), (200, 256, 1024),
+                                   (16, 151936, 1024)])
+def test_noalloc_matches_workspace_entry_point(m, n, k):
+    from blackwell_ops import _lib
+
+    lib = _lib.lib
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    st = _lib.stream_ptr(dev)
+    g = torch.Generator(device=dev).manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, generator=g, device=dev).half()
+    q = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
+    s = (torch.rand(n, generator=g, device=dev) * 1e-3 + 1e-4).half()
+    ref, need = _gemm_with_workspace(lib, st, x, q, s, m, n, k)
+    assert need <= lib.bw_w8a16_gemm_static_scratch_bytes()
+    for _ in range(2):
+        y = torch.full((m, n), float("nan"), dtype=torch.float16, device=dev)
+        rc = lib.bw_w8a16_gemm_noalloc(x.data_ptr(), 0, k, q.data_ptr(), k, s.data_ptr(), 0, y.data_ptr(), n, m, n,
+                                       k, st)
+        assert rc == 0, lib.bw_last_error()
+        torch.cuda.synchronize()
+        err = (y.double() - ref.double()).abs()
+        assert float(err.max()) <= 1e-2
+        assert float(err.norm() / ref.double().norm()) <= 1e-3
+    assert _lib.device_status() == 0
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch():
+    from blackwell_ops import _lib
+
+    lib = _lib.lib
+    dev = torch.device("cuda:0")
+    limit = lib.bw_w8a16_gemm_static_scratch_bytes()
+    candidates = [(m, n, k) for m in (128, 96, 64) for n in (8192, 4096, 2048) for k in (65536, 131072, 262144)]
+    over = [c for c in candidates if lib.bw_w8a16_gemm_workspace_size(*c) > limit]
+    assert over, "no candidate shape needs more split-K scratch than the static array"
+    m, n, k = min(over, key=lambda c: c[0] * c[2] + c[1] * c[2])
+    x = torch.zeros(m, k, dtype=torch.float16, device=dev)
+    q = torch.zeros(n, k, dtype=torch.int8, device=dev)
+    s = torch.ones(n, dtype=torch.float16, device=dev)
+    y = torch.empty(m, n, dtype=torch.float16, device=dev)
+    rc = lib.bw_w8a16_gemm_noalloc(x.data_ptr(), 0, k, q.data_ptr(), k, s.data_ptr(), 0, y.data_ptr(), n, m, n, k,
+                                   _lib.stream_ptr(dev))
+    assert rc == _lib.BW_ERR_WORKSPACE
+    assert b"static array" in lib.bw_last_error()
