@@ -154,7 +154,7 @@ class MergeRequantWorkload:
     """cfg2: LoRA delta + merge + requant for one Qwen3-0.6B layer, r in {16, 128}, per step."""
 
     name = "cfg2"
-    kernel = "lora_tc_kernel<requant>"
+    kernel = "lora_requant_cluster_kernel"
     unit = "TFLOPS"
     metric_kind = "tflops"
     ranks_r = (16, 128)
@@ -179,7 +179,20 @@ class MergeRequantWorkload:
                            for r in self.ranks_r})
         self.flops = sum(2.0 * r * n * k for r in self.ranks_r for _, k, n in QWEN)
         self.bytes = sum(2 * n * k + 2 * r * (n + k) + n * k + 2 * n for r in self.ranks_r for _, k, n in QWEN)
-        self.launches_per_step = len(self.ranks_r) * len(QWEN)
+        # one batched call per (layer, adapter): all 7 projections in one launch
+        from blackwell_ops._lib import RequantProblem
+
+        self.problems = []
+        for li in range(layers):
+            per_r = {}
+            for r in self.ranks_r:
+                arr = (RequantProblem * len(QWEN))(*[
+                    RequantProblem(self.W[li][p].data_ptr(), k, self.A[li][r][p].data_ptr(),
+                                   self.B[li][r][p].data_ptr(), 2.0, self.Q[li][r][p].data_ptr(), k,
+                                   self.S[li][r][p].data_ptr(), n, k, r) for p, (_, k, n) in enumerate(QWEN)])
+                per_r[r] = arr
+            self.problems.append(per_r)
+        self.launches_per_step = len(self.ranks_r)
 
     def config(self):
         return workload_config("cfg2", 0)
@@ -189,18 +202,9 @@ class MergeRequantWorkload:
     def step(self, s, st, events=None):
         li = s % self.layers
         for r in self.ranks_r:
-            for p, (_, k, n) in enumerate(QWEN):
-                if events is not None:
-                    events.append(torch.cuda.Event(enable_timing=True))
-                    events[-1].record()
-                rc = self.lib.bw_lora_merge_requant(
-                    self.W[li][p].data_ptr(), k, self.A[li][r][p].data_ptr(), self.B[li][r][p].data_ptr(), 2.0,
-                    self.Q[li][r][p].data_ptr(), k, self.S[li][r][p].data_ptr(), n, k, r, st)
-                if events is not None:
-                    events.append(torch.cuda.Event(enable_timing=True))
-                    events[-1].record()
-                if rc:
-                    raise RuntimeError(self.lib.bw_last_error().decode())
+            rc = self.lib.bw_lora_merge_requant_batched(self.problems[li][r], len(QWEN), st)
+            if rc:
+                raise RuntimeError(self.lib.bw_last_error().decode())
 
     # -- end to end through the public API with host (pinned) buffers --
     def e2e_setup(self):
@@ -217,14 +221,14 @@ class MergeRequantWorkload:
         self.d2h = sum(n * k + 2 * n for _ in self.ranks_r for _, k, n in QWEN)
 
     def e2e_step(self, s):
-        from blackwell_ops.cuda import lora_merge_requant
+        from blackwell_ops.cuda import lora_merge_requant_batched
 
         W = [t.to(self.dev, non_blocking=True) for t in self.hW]
         for r in self.ranks_r:
-            for p in range(len(QWEN)):
-                A = self.hA[r][p].to(self.dev, non_blocking=True)
-                B = self.hB[r][p].to(self.dev, non_blocking=True)
-                q, sc = lora_merge_requant(W[p], A, B, 2.0)
+            A = [t.to(self.dev, non_blocking=True) for t in self.hA[r]]
+            B = [t.to(self.dev, non_blocking=True) for t in self.hB[r]]
+            outs = lora_merge_requant_batched(zip(W, A, B, [2.0] * len(QWEN)))
+            for p, (q, sc) in enumerate(outs):
                 self.hQ[r][p].copy_(q, non_blocking=True)
                 self.hS[r][p].copy_(sc, non_blocking=True)
 
@@ -342,8 +346,8 @@ class GemmSweepWorkload:
 
         i = step_index % len(self.shapes)
         k, n = self.shapes[i]
-        if self.name == "cfg4":
-            n = min(n, 1024)  # bounded sample: a 1024-column slice of the projection
+        if self.name in ("cfg4", "cfg5"):
+            n = min(n, 1024)  # bounded sample: a 1024-row slice of the projection
         g = torch.Generator().manual_seed(step_index)
         w = (torch.randn((n, k), generator=g) * 0.02).to(self.xdtype)
         q, s = torch_port.quantize_weight_int8(w)
@@ -355,6 +359,182 @@ class GemmSweepWorkload:
         return amount, dt, f"one projection per step ({n}x{k}, M={self.m})"
 
 
+class QuantizeWorkload:
+    """quant: per-channel int8 quantisation of weights (quantize_weight_int8), HBM-bound.
+
+    One step quantises the Llama-3-8B MLP weights (14336x4096 and 4096x14336, bf16)
+    of one of 4 rotating layers (940 MB > L2).  Metric GB/s."""
+
+    kernel = "quantize_rows_reg_kernel"
+    name = "quant"
+    metric_kind = "gbs"
+    unit = "GB/s"
+
+    def __init__(self, dev, rank, world):
+        from blackwell_ops import _lib
+
+        self.lib = _lib.lib
+        self.dev = dev
+        self.xdtype = torch.bfloat16
+        g = torch.Generator(device=dev).manual_seed(3000 + rank)
+        self.layers = 4
+        self.W = [[randn((n, k), 0.02, torch.bfloat16, g, dev) for k, n in LLAMA8B_MLP] for _ in range(self.layers)]
+        self.Q = [[torch.empty((n, k), dtype=torch.int8, device=dev) for k, n in LLAMA8B_MLP] for _ in range(self.layers)]
+        self.S = [[torch.empty((n,), dtype=torch.bfloat16, device=dev) for k, n in LLAMA8B_MLP] for _ in range(self.layers)]
+        self.bytes = sum(2 * n * k + n * k + 2 * n for k, n in LLAMA8B_MLP)
+        self.flops = 0.0
+        self.variants = self.layers
+        self.launches_per_step = len(LLAMA8B_MLP)
+
+    def config(self):
+        return workload_config("quant", 0)
+
+    def step(self, s, st, events=None):
+        li = s % self.layers
+        for j, (k, n) in enumerate(LLAMA8B_MLP):
+            rc = self.lib.bw_quantize_rowwise_int8(self.W[li][j].data_ptr(), 1, n, k, k, self.Q[li][j].data_ptr(), k,
+                                                   self.S[li][j].data_ptr(), st)
+            if rc:
+                raise RuntimeError(self.lib.bw_last_error().decode())
+
+    def e2e_setup(self):
+        g = torch.Generator().manual_seed(4)
+        self.hW = [(torch.randn((n, k), generator=g) * 0.02).bfloat16().pin_memory() for k, n in LLAMA8B_MLP]
+        self.hQ = [torch.empty((n, k), dtype=torch.int8).pin_memory() for k, n in LLAMA8B_MLP]
+        self.h2d = sum(t.numel() * 2 for t in self.hW)
+        self.d2h = sum(n * k + 2 * n for k, n in LLAMA8B_MLP)
+
+    def e2e_step(self, s):
+        from blackwell_ops.kernels import quantize_weight_int8
+
+        for j in range(len(LLAMA8B_MLP)):
+            q, _ = quantize_weight_int8(self.hW[j].to(self.dev, non_blocking=True))
+            self.hQ[j].copy_(q, non_blocking=True)
+
+    @staticmethod
+    def cpu_sample(step_index: int):
+        from oracle import torch_port
+
+        k, n = LLAMA8B_MLP[step_index % 2]
+        n = 1024
+        g = torch.Generator().manual_seed(step_index)
+        w = (torch.randn((n, k), generator=g) * 0.02).bfloat16()
+        t0 = time.perf_counter()
+        torch_port.quantize_weight_int8(w)
+        return 2 * n * k + n * k + 2 * n, time.perf_counter() - t0, f"1024-row slice of a Llama-3-8B MLP weight (K={k})"
+
+
+class NSplitWorkload:
+    """cfg5: Llama-3-70B MLP W8A16 with 32 adapter int8 copies, column-parallel over the ranks.
+
+    Setup (adapter load time, not timed): every adapter (r drawn from {16, 64, 128})
+    is merged into its own int8 copy of this rank's row shard with
+    ``lora_merge_requant_batched``.  A step serves one adapter (round robin):
+    the local W8A16 GEMM of each projection writes this rank's slice, NCCL
+    all-gathers the slices over NVLink and they are laid out as [M, N].
+    """
+
+    kernel = "w8a16_persistent_kernel"
+    name = "cfg5"
+
+    def __init__(self, dev, rank, world, m, adapters=32, group=None):
+        from blackwell_ops import _lib
+        from blackwell_ops.cuda import lora_merge_requant_batched
+        from blackwell_ops.nsplit import shard_rows
+
+        self.lib = _lib.lib
+        self.dev, self.rank, self.world, self.m = dev, rank, world, m
+        self.group = group
+        self.xdtype = torch.bfloat16
+        self.shapes = LLAMA70B_MLP  # (K, N)
+        g = torch.Generator(device=dev).manual_seed(5000 + rank)
+        gr = torch.Generator().manual_seed(77)
+        self.ranks_r = [int(v) for v in torch.tensor([16, 64, 128])[torch.randint(0, 3, (adapters,), generator=gr)]]
+        self.per = [-(-n // world) for _, n in self.shapes]
+        self.Q, self.S = [], []  # [adapter][proj]
+        base = []
+        for (k, n), per in zip(self.shapes, self.per):
+            a, b = shard_rows(n, world, rank)
+            w = torch.zeros((per, k), dtype=torch.float16, device=dev)
+            w[: b - a] = randn((b - a, k), 0.02, torch.float16, g, dev)
+            base.append(w)
+        for ai, r in enumerate(self.ranks_r):
+            items = []
+            for (k, n), per, w in zip(self.shapes, self.per, base):
+                A = randn((r, k), 1.0 / math.sqrt(k), torch.float16, g, dev)
+                B = randn((per, r), 0.01, torch.float16, g, dev)
+                items.append((w, A, B, 2.0))
+            outs = lora_merge_requant_batched(items)
+            self.Q.append([q for q, _ in outs])
+            self.S.append([s for _, s in outs])
+        del base
+        torch.cuda.synchronize()
+        self.X = [randn((m, k), 1.0, self.xdtype, g, dev) for k, _ in self.shapes]
+        self.Yloc = [torch.empty((m, per), dtype=self.xdtype, device=dev) for per in self.per]
+        self.Ygat = [torch.empty((world, m, per), dtype=self.xdtype, device=dev) for per in self.per]
+        self.Y = [torch.empty((m, n), dtype=self.xdtype, device=dev) for _, n in self.shapes]
+        ws = max(self.lib.bw_w8a16_gemm_workspace_size(m, per, k) for (k, _), per in zip(self.shapes, self.per))
+        self.ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.variants = len(self.ranks_r)
+        self.launches_per_step = len(self.shapes)
+        self.metric_kind = "gbs" if m < 512 else "tflops"
+        self.unit = "GB/s" if m < 512 else "TFLOPS"
+        # whole-job algorithmic work of one step (all ranks together)
+        self.bytes_total = sum(n * k + 2 * n + 2 * m * k + 2 * m * n for k, n in self.shapes)
+        self.flops_total = sum(2.0 * m * n * k for k, n in self.shapes)
+        # this rank's local GEMM work (for the per-kernel roofline)
+        self.bytes = sum(per * k + 2 * per + 2 * m * k + 2 * m * per for (k, _), per in zip(self.shapes, self.per))
+        self.flops = sum(2.0 * m * per * k for (k, _), per in zip(self.shapes, self.per))
+
+    def config(self):
+        return workload_config("cfg5", self.m) | {"gpus": self.world}
+
+    def step(self, s, st, events=None):
+        ai = s % len(self.ranks_r)
+        for j, ((k, n), per) in enumerate(zip(self.shapes, self.per)):
+            rc = self.lib.bw_w8a16_gemm(self.X[j].data_ptr(), 1, k, self.Q[ai][j].data_ptr(), k,
+                                        self.S[ai][j].data_ptr(), 0, self.Yloc[j].data_ptr(), per, self.m, per, k,
+                                        self.ws.data_ptr(), self.ws.numel(), st)
+            if rc:
+                raise RuntimeError(self.lib.bw_last_error().decode())
+            if self.world > 1:
+                dist.all_gather_into_tensor(self.Ygat[j], self.Yloc[j], group=self.group)
+                self.Y[j].copy_(self.Ygat[j].permute(1, 0, 2).reshape(self.m, self.world * per)[:, :n])
+            else:
+                self.Y[j].copy_(self.Yloc[j][:, :n])
+
+    def e2e_setup(self):
+        g = torch.Generator().manual_seed(9)
+        self.hX = [torch.randn(x.shape, generator=g).to(self.xdtype).pin_memory() for x in self.X]
+        self.hY = [torch.empty(y.shape, dtype=self.xdtype).pin_memory() for y in self.Y]
+        self.h2d = sum(x.numel() * 2 for x in self.hX)
+        self.d2h = sum(y.numel() * 2 for y in self.hY)
+
+    def e2e_step(self, s):
+        from blackwell_ops.nsplit import ColumnParallelW8A16
+
+        ai = s % len(self.ranks_r)
+        for j, (k, n) in enumerate(self.shapes):
+            x = self.hX[j].to(self.dev, non_blocking=True)
+            layer = ColumnParallelW8A16(self.Q[ai][j], self.S[ai][j], n, group=self.group)
+            self.hY[j].copy_(layer(x), non_blocking=True)
+
+    def cpu_sample(self, step_index: int):
+        from oracle import torch_port
+
+        k, n = self.shapes[step_index % 2]
+        n = 1024  # bounded sample: a 1024-row slice of the projection
+        g = torch.Generator().manual_seed(step_index)
+        w = (torch.randn((n, k), generator=g) * 0.02).half()
+        q, s = torch_port.quantize_weight_int8(w)
+        x = torch.randn((self.m, k), generator=g).to(self.xdtype)
+        t0 = time.perf_counter()
+        torch_port.int8_gemm(x, q, s)
+        dt = time.perf_counter() - t0
+        amount = (2.0 * self.m * n * k) if self.metric_kind == "tflops" else (n * k + 2 * n + 2 * self.m * (k + n))
+        return amount, dt, f"1024-row slice of a 70B MLP projection per step (K={k}, M={self.m})"
+
+
 # ---------------------------------------------------------------------------
 # main
 # ---------------------------------------------------------------------------
@@ -364,6 +544,10 @@ def make_workload(args, dev, rank, world):
     if args.workload in ("cfg1", "cfg3", "cfg4"):
         m = args.m if args.m else {"cfg1": 16, "cfg3": 16, "cfg4": 2048}[args.workload]
         return GemmSweepWorkload(args.workload, dev, rank, world, m)
+    if args.workload == "quant":
+        return QuantizeWorkload(dev, rank, world)
+    if args.workload == "cfg5":
+        return NSplitWorkload(dev, rank, world, args.m if args.m else 16, adapters=args.adapters)
     raise SystemExit(f"unknown workload {args.workload}")
 
 
@@ -384,6 +568,9 @@ def run_reference(args, rank, world):
     if args.workload == "cfg2":
         sample = MergeRequantWorkload.cpu_sample
         kind, unit = "tflops", "TFLOPS"
+    elif args.workload == "quant":
+        sample = QuantizeWorkload.cpu_sample
+        kind, unit = "gbs", "GB/s"
     else:
         wl_cpu = GemmCpuShim(args)
         sample, kind, unit = wl_cpu.cpu_sample, wl_cpu.metric_kind, wl_cpu.unit
@@ -397,7 +584,8 @@ def run_reference(args, rank, world):
     v = scale_unit(tot, secs, kind)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 6), "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16" if args.workload != "cfg4" else "bf16",
+            "higher_is_better": True, "scaling": "strong" if args.workload == "cfg5" else "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.workload in ("cfg4", "cfg5") else "f16",
             "data": "synthetic (seeded), random-init weights",
             "config": config_for(args),
             "cpu_baseline": {"value": round(v, 6), "unit": unit, "cores": cores, "kind": "port", "sample": desc},
@@ -410,27 +598,34 @@ class GemmCpuShim:
 
     def __init__(self, args):
         self.name = args.workload
-        self.m = args.m if args.m else {"cfg1": 16, "cfg3": 16, "cfg4": 2048}.get(args.workload, 16)
+        self.m = args.m if args.m else DEFAULT_M.get(args.workload, 16)
         self.xdtype = torch.bfloat16 if self.name == "cfg4" else torch.float16
         if self.name == "cfg1":
             self.shapes = [(1024, 3072)]
         elif self.name == "cfg3":
             self.shapes = [(k, n) for _, k, n in QWEN] + [LM_HEAD]
+        elif self.name == "cfg5":
+            self.shapes = list(LLAMA70B_MLP)
+            self.xdtype = torch.bfloat16
         else:
             self.shapes = list(LLAMA8B_MLP)
-        self.metric_kind = "tflops" if self.name == "cfg4" else "gbs"
-        self.unit = "TFLOPS" if self.name == "cfg4" else "GB/s"
+        big_m = self.name == "cfg4" or (self.name == "cfg5" and self.m >= 512)
+        self.metric_kind = "tflops" if big_m else "gbs"
+        self.unit = "TFLOPS" if big_m else "GB/s"
 
     cpu_sample = GemmSweepWorkload.cpu_sample
 
 
 METRIC = "W8A16 GEMM HBM GB/s (decode) / TFLOPS (prefill, ΔW) vs B200 roofline"
 
-DEFAULT_M = {"cfg1": 16, "cfg3": 16, "cfg4": 2048}
+DEFAULT_M = {"cfg1": 16, "cfg3": 16, "cfg4": 2048, "cfg5": 16}
 
 
 def workload_config(name: str, m: int) -> dict:
     """The `config` object of the JSON line; identical for both arms."""
+    if name == "quant":
+        return {"workload": "quant: quantize_weight_int8 of Llama-3-8B MLP weights (14336x4096, 4096x14336), bf16",
+                "l2": "inputs larger than L2 (4 rotating layers, 940 MB)", "parallelism": "weak: independent replicas"}
     if name == "cfg2":
         return {"workload": "cfg2: LoRA delta+merge+requant, Qwen3-0.6B layer (7 projections), r in {16,128}, "
                             "alpha=2r (scaling 2)", "layers_rotated": QWEN_LAYERS,
@@ -440,7 +635,12 @@ def workload_config(name: str, m: int) -> dict:
     desc = {"cfg1": "cfg1: W8A16 GEMM X[16,1024] x W[3072,1024]^T, fp16; one step = 64 GEMMs on 64 distinct "
                     "weight copies (210 MB > L2)",
             "cfg3": f"cfg3: Qwen3-0.6B decode sweep, 28 layers x 7 projections + LM head, M={m}, fp16",
-            "cfg4": f"cfg4: Llama-3-8B MLP prefill W8A16 (4096->14336, 14336->4096), M={m}, bf16"}[name]
+            "cfg4": f"cfg4: Llama-3-8B MLP prefill W8A16 (4096->14336, 14336->4096), M={m}, bf16",
+            "cfg5": f"cfg5: Llama-3-70B MLP W8A16 (8192->28672, 28672->8192), 32 adapter int8 copies "
+                    f"(r in {{16,64,128}}), M={m}, bf16"}[name]
+    if name == "cfg5":
+        return {"workload": desc, "m": m, "l2": "inputs larger than L2 (470 MB of int8 weights per adapter step)",
+                "parallelism": "column-parallel N-split over the GPUs, NCCL all-gather of output slices (strong)"}
     return {"workload": desc, "m": m, "l2": "inputs larger than L2 (weights streamed from HBM each step)",
             "parallelism": "weak: independent replicas per rank"}
 
@@ -457,6 +657,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="cfg2")
     ap.add_argument("--m", type=int, default=0, help="tokens for the GEMM workloads")
+    ap.add_argument("--adapters", type=int, default=32, help="cfg5: number of adapters")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -544,7 +745,11 @@ def main():
     kern_ms_per_step = kern_ms / args.steps
 
     amount = amount_of(wl)
-    value = scale_unit(amount * world, ms_max / args.steps / 1e3, wl.metric_kind)
+    if wl.name == "cfg5":  # strong scaling: the job's work is fixed, shared by the ranks
+        amount = wl.flops_total if wl.metric_kind == "tflops" else wl.bytes_total
+        value = scale_unit(amount, ms_max / args.steps / 1e3, wl.metric_kind)
+    else:
+        value = scale_unit(amount * world, ms_max / args.steps / 1e3, wl.metric_kind)
     achieved_gbs = wl.bytes / (kern_ms_per_step / 1e3) / 1e9
     achieved_tf = wl.flops / (kern_ms_per_step / 1e3) / 1e12
     if wl.name == "cfg4" or (wl.name in ("cfg5",) and wl.metric_kind == "tflops"):
@@ -578,7 +783,8 @@ def main():
         torch.cuda.synchronize()
         barrier()
         e_ms = max_over_ranks(e0.elapsed_time(e1))
-        e2e = {"value": round(scale_unit(amount * world, e_ms / args.steps / 1e3, wl.metric_kind), 4),
+        e2e_amount = amount if wl.name == "cfg5" else amount * world
+        e2e = {"value": round(scale_unit(e2e_amount, e_ms / args.steps / 1e3, wl.metric_kind), 4),
                "unit": wl.unit, "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
                "ms_per_step": round(e_ms / args.steps, 4)}
 
@@ -599,10 +805,12 @@ def main():
         cpu = {"value": round(scale_unit(tot, secs, wl.metric_kind), 6), "unit": wl.unit,
                "cores": torch.get_num_threads(), "kind": "port", "sample": desc + f", {i - 1} samples"}
 
+    graphs.clear()  # graphs holding NCCL work are released before the process group
+    torch.cuda.synchronize()
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 4), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None,
+                "scaling": "strong" if wl.name == "cfg5" else "weak", "vs_baseline": None,
                 "dtype": "bf16" if getattr(wl, "xdtype", torch.float16) == torch.bfloat16 else "f16",
                 "data": "synthetic (seeded), random-init weights", "config": wl.config(), "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": wl.launches_per_step * args.steps,

@@ -182,15 +182,26 @@ class MultiDeltaLoRAModel:
         else:
             entries = dict(adapter)
         used: dict[str, tuple[torch.Tensor, torch.Tensor, float]] = {}
-        for layer_name, layer in self._lora_layers.items():
+        for layer_name in self._lora_layers:
             if layer_name not in entries:
                 continue
             A, B, scaling = entries[layer_name]
             A = A.to(self.device, torch.float16).contiguous()
             B = B.to(self.device, torch.float16).contiguous()
-            if self.quantize:
-                layer.add_adapter(name, A, B, float(scaling))
             used[layer_name] = (A, B, float(scaling))
+        if self.quantize and used:
+            # every projection of the adapter merged + requantised in batched launches
+            from blackwell_ops.cuda import lora_merge_requant_batched
+
+            names = list(used)
+            layers = [self._lora_layers[n] for n in names]
+            for layer in layers:
+                if layer.base_weight is None:
+                    raise RuntimeError("a layer was built without its fp16 base weight; cannot merge adapters")
+            outs = lora_merge_requant_batched(
+                (layer.base_weight, used[n][0], used[n][1], used[n][2]) for n, layer in zip(names, layers))
+            for layer, (q, s) in zip(layers, outs):
+                layer.copies[name] = (q, s)
         self._adapters[name] = used
         if self._current_adapter == name:  # reloaded while active: re-apply
             self._current_adapter = None

@@ -28,6 +28,15 @@ DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 _c = ctypes
 _P = _c.c_void_p
 _I64 = _c.c_int64
+
+
+class RequantProblem(ctypes.Structure):
+    """Mirror of bw_lora_requant_problem (include/bw_ops.h)."""
+
+    _fields_ = [("w", _P), ("ldw", _I64), ("a", _P), ("b", _P), ("scaling", _c.c_float), ("q", _P),
+                ("ldq", _I64), ("scale", _P), ("n", _I64), ("k", _I64), ("r", _I64)]
+
+
 SIGNATURES = {
     "bw_status_string": (_c.c_char_p, [_c.c_int]),
     "bw_last_error": (_c.c_char_p, []),
@@ -44,6 +53,7 @@ SIGNATURES = {
     "bw_add_delta": (_c.c_int, [_P, _P, _I64, _P]),
     "bw_lora_merge": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),
     "bw_lora_merge_requant": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _P, _I64, _I64, _I64, _P]),
+    "bw_lora_merge_requant_batched": (_c.c_int, [_c.POINTER(RequantProblem), _c.c_int, _P]),
     "bw_device_status": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_int), _P]),
 }
 

@@ -23,7 +23,7 @@ from __future__ import annotations
 
 import torch
 
-from .._lib import check, lib, stream_ptr
+from .._lib import RequantProblem, check, lib, stream_ptr
 
 
 def _check_ab(A: torch.Tensor, B: torch.Tensor) -> tuple[int, int, int]:
@@ -134,4 +134,49 @@ def lora_merge_requant(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
     return q, scale
 
 
-__all__ = ["lora_delta", "lora_delta_tiled", "add_delta_", "lora_merge", "lora_merge_requant"]
+def lora_merge_requant_batched(items):
+    """Fused merge + requantisation of several projections in as few launches as possible.
+
+    ``items``: iterable of ``(W, A, B, scaling)`` on one device.  Returns a list
+    of ``(w_int8, scale)``, each equal to ``lora_merge_requant(W, A, B, scaling)``.
+    """
+    items = list(items)
+    if not items:
+        return []
+    keep, outs, probs = [], [], []
+    dev = None
+    for W, A, B, scaling in items:
+        r, K, N = _check_ab(A, B)
+        W = _check_w(W, N, K)
+        if K == 0:
+            raise RuntimeError("lora_merge_requant: Expected reduction dim -1 to have non-zero size")
+        if dev is None:
+            dev = W.device
+        elif W.device != dev:
+            raise RuntimeError("lora_merge_requant_batched: all problems must be on one device")
+        A = A.contiguous()
+        B = B.contiguous()
+        q = torch.empty((N, K), dtype=torch.int8, device=dev)
+        sc = torch.empty((N,), dtype=torch.float16, device=dev)
+        outs.append((q, sc))
+        if N == 0:
+            continue
+        if r == 0:
+            from ..kernels import quantize_weight_int8
+
+            q2, s2 = quantize_weight_int8(W)
+            q.copy_(q2)
+            sc.copy_(s2)
+            continue
+        keep.append((W, A, B))
+        probs.append(RequantProblem(W.data_ptr(), W.stride(0), A.data_ptr(), B.data_ptr(), float(scaling),
+                                    q.data_ptr(), K, sc.data_ptr(), N, K, r))
+    if probs:
+        arr = (RequantProblem * len(probs))(*probs)
+        with torch.cuda.device(dev):
+            check(lib.bw_lora_merge_requant_batched(arr, len(probs), stream_ptr(dev)), "lora_merge_requant_batched")
+    return outs
+
+
+__all__ = ["lora_delta", "lora_delta_tiled", "add_delta_", "lora_merge", "lora_merge_requant",
+           "lora_merge_requant_batched"]

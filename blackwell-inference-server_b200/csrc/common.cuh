@@ -71,16 +71,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// records `site`) if it did not within BW_WAIT_LIMIT_NS, or if another thread
-// of the CTA has already flagged an abort through `abort_flag`.
+// records `site`) if it did not within BW_WAIT_LIMIT_NS (measured with the SM
+// cycle counter, assuming at most 2.5 GHz so the bound is never shorter), or if
+// another thread of the CTA has already flagged an abort through `abort_flag`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int site) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;  // cycles
+  const long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 31u) == 0u) {
+    if ((i & 63u) == 0u) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer() - t0 > BW_WAIT_LIMIT_NS) {
+      if (clock64() - t0 > limit) {
         record_timeout(site);
         if (abort_flag != nullptr) *abort_flag = 1;
         return false;
@@ -129,15 +131,38 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   int site) {
-  const uint64_t t0 = globaltimer();
+  const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
+  const long long t0 = clock64();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 31u) == 31u && globaltimer() - t0 > BW_WAIT_LIMIT_NS) {
+    if ((i & 63u) == 63u && clock64() - t0 > limit) {
       record_timeout(site);
       if (abort_flag != nullptr) *abort_flag = 1;
       return false;
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// named barriers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Named barrier that also ORs a predicate over the participating threads, so
+// every participant takes the same abort decision (a thread that left a loop
+// alone would otherwise leave its siblings waiting at a later bar.sync).
+__device__ __forceinline__ bool named_bar_any(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -263,6 +288,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
 }

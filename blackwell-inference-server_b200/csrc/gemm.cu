@@ -65,25 +65,6 @@ struct GemmCfg {
   static_assert((2 * STAGES + 2 * ASTAGES + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
 };
 
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-// Named barrier that also ORs a predicate over the participating threads, so
-// every participant takes the same abort decision (a thread that left a loop
-// alone would otherwise leave its siblings waiting at a later bar.sync).
-__device__ __forceinline__ bool named_bar_any(int id, int nthreads, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
-      : "memory");
-  return r != 0;
-}
-
 template <bool BF16>
 __device__ __forceinline__ void convert_chunk(const uint4& v, uint4& o0, uint4& o1) {
   if constexpr (BF16) {
@@ -325,9 +306,9 @@ __global__ void __launch_bounds__(192, 1)
 // the weight stream never drains between tiles.  448 threads:
 //   warp 0       TMA producer (STAGES-deep ring of [W int8 128x128 B | x BM x 128])
 //   warp 1       TMEM owner (512 columns) + tcgen05.mma issuer
-//   warps 2-9    dequantisers: thread = weight row, warps 2-5 take k columns
-//                0-63 and warps 6-9 columns 64-127 of a stage; int8 -> f16/bf16
-//                straight into a TMEM A buffer (tcgen05.st), 4 buffers x 64 cols
+//   warps 2-9    dequantisers in two groups of four that take alternate k-blocks
+//                (thread = weight row, all 128 columns of the stage); int8 ->
+//                f16/bf16 straight into a TMEM A buffer (tcgen05.st), 4 x 64 cols
 //   warps 10-13  epilogue: double-buffered TMEM accumulators (2 x BM cols), so a
 //                unit's epilogue overlaps the next unit's mainloop
 // The MMA is the TS form: A (dequantised W) from TMEM, B (x) from shared memory.
@@ -401,10 +382,10 @@ __global__ void __launch_bounds__(448, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 8 + 1);  // 8 dequantiser warps + 1 MMA commit
+      mbar_init(&empty[s], 4 + 1);  // one group of 4 dequantiser warps + 1 MMA commit
     }
     for (int t = 0; t < ASTAGES; ++t) {
-      mbar_init(&afull[t], 8);
+      mbar_init(&afull[t], 4);
       mbar_init(&aempty[t], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -532,11 +513,13 @@ __global__ void __launch_bounds__(448, 1)
     }
   } else if (warp < 10) {
     // ---------------- dequantisers ----------------
+    // Two groups of four warps take alternate k-blocks, so two stages are
+    // dequantised at once; within a group, thread = weight row (all 128 columns).
     const int q = warp & 3;
-    const int h = (warp - 2) >> 2;
+    const int grp = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const int sw = row & 7;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::A_COL0 + h * 32;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::A_COL0;
     int it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -544,6 +527,7 @@ __global__ void __launch_bounds__(448, 1)
       const int kb0 = sp * kb_per_split;
       const int nkb = min(kb_per_split, kblocks - kb0);
       for (int i = 0; i < nkb; ++i, ++it) {
+        if ((it & 1) != grp) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         const int t = it % ASTAGES;
@@ -555,24 +539,27 @@ __global__ void __launch_bounds__(448, 1)
         }
         tc_fence_after();
         const uint8_t* src = sW + s * C::W_BYTES + row * 128;
-        uint4 v[4];
+        uint4 v[8];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) v[c] = *reinterpret_cast<const uint4*>(src + (((4 * h + c) ^ sw) << 4));
-        uint32_t out[32];
+        for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 o0, o1;
-          convert_chunk<BF16>(v[c], o0, o1);
-          out[8 * c + 0] = o0.x;
-          out[8 * c + 1] = o0.y;
-          out[8 * c + 2] = o0.z;
-          out[8 * c + 3] = o0.w;
-          out[8 * c + 4] = o1.x;
-          out[8 * c + 5] = o1.y;
-          out[8 * c + 6] = o1.z;
-          out[8 * c + 7] = o1.w;
+        for (int h = 0; h < 2; ++h) {
+          uint32_t out[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 o0, o1;
+            convert_chunk<BF16>(v[4 * h + c], o0, o1);
+            out[8 * c + 0] = o0.x;
+            out[8 * c + 1] = o0.y;
+            out[8 * c + 2] = o0.z;
+            out[8 * c + 3] = o0.w;
+            out[8 * c + 4] = o1.x;
+            out[8 * c + 5] = o1.y;
+            out[8 * c + 6] = o1.z;
+            out[8 * c + 7] = o1.w;
+          }
+          tmem_st32(lane_base + t * 64 + h * 32, out);
         }
-        tmem_st32(lane_base + t * 64, out);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();

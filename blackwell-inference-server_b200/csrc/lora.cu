@@ -30,7 +30,11 @@
 // codes.  The merged fp16 weight never touches HBM.
 #include <stdio.h>
 
+#include <string.h>
+
+#include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "quant_math.cuh"
 
@@ -281,6 +285,254 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
+// Grouped merge + requantisation, one cluster per 128-row block (K <= 4096).
+//
+// One launch covers up to kReqMaxProblems projections (e.g. every projection an
+// adapter touches).  A cluster of C CTAs (C <= 16) owns one 128-row block of one
+// problem; CTA c owns columns [c*Kc, (c+1)*Kc), Kc <= 256, and:
+//   1. TMA-loads B[128 rows, r], its A[r, Kc] slice and its W[128, Kc] slice
+//      once (W is read from HBM exactly once);
+//   2. per 64-column panel: tcgen05.mma (M=128, N=64, K=16 x r/16) into one of
+//      two TMEM accumulators; 8 epilogue warps merge W' = fp16(W + fp16(acc*s))
+//      IN PLACE in shared memory (__hadd2 is the correctly rounded fp16 sum,
+//      which equals fp16(fp32(W) + fp32(delta)) for fp16 operands) and track
+//      the row's |W'| maximum;
+//   3. push the per-row maxima to every CTA of the cluster through distributed
+//      shared memory (bounded mbarrier wait), reduce, derive the scale;
+//   4. quantise the resident merged slice in place (fast exact quantiser) and
+//      TMA-store int8 panels (64-byte swizzle).
+// The merged weight never leaves the SM; no scratch memory.
+// ---------------------------------------------------------------------------
+constexpr int kReqMaxProblems = 16;
+constexpr int kReqMaxCluster = 16;
+constexpr int kReqThreads = 320;  // warp 0 TMA, warp 1 MMA/TMEM, warps 2-9 epilogue
+
+struct ReqProblem {
+  __half* scale;
+  float s;
+  int n, k, r, rp, nbp, kc, rb0;  // rp: r rounded to 16; kc: columns per CTA; rb0: first row block
+};
+
+struct ReqBatch {
+  CUtensorMap tm_w[kReqMaxProblems];
+  CUtensorMap tm_a[kReqMaxProblems];
+  CUtensorMap tm_b[kReqMaxProblems];
+  CUtensorMap tm_q[kReqMaxProblems];
+  ReqProblem p[kReqMaxProblems];
+  int count;
+  int total_rb;
+  int cluster;
+  // shared-memory carve-up (bytes, 1024-aligned), sized for the largest problem
+  int off_a, off_w, off_red, off_bar;
+};
+
+enum ReqWaitSite : int { kSiteReqLoad = 211, kSiteReqD = 212, kSiteReqDE = 213, kSiteReqX = 214, kSiteReqFinal = 215 };
+
+__global__ void __launch_bounds__(kReqThreads, 1) lora_requant_cluster_kernel(const __grid_constant__ ReqBatch batch) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;
+  uint8_t* sA = smem + batch.off_a;
+  uint8_t* sW = smem + batch.off_w;
+  float* red = reinterpret_cast<float*>(smem + batch.off_red);  // [2][128] per-half maxima
+  float* xred = red + 256;                                       // [C][128] cluster maxima
+  uint64_t* bar_load = reinterpret_cast<uint64_t*>(smem + batch.off_bar);
+  uint64_t* dfull = bar_load + 1;    // 2
+  uint64_t* dempty = dfull + 2;      // 2
+  uint64_t* bar_x = dempty + 2;
+  uint64_t* final_bar = bar_x + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int C = static_cast<int>(gridDim.x);
+  const int rank = static_cast<int>(cluster_ctarank());
+
+  // which problem / row block this cluster owns
+  const int rb_global = blockIdx.y;
+  int pi = 0;
+  while (pi + 1 < batch.count && batch.p[pi + 1].rb0 <= rb_global) ++pi;
+  const ReqProblem& P = batch.p[pi];
+  const int n0 = (rb_global - P.rb0) * 128;
+  const int k_begin = rank * P.kc;
+  const int k_len = max(0, min(P.kc, P.k - k_begin));
+  const int npanel = (k_len + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_load, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&dfull[b], 1);
+      mbar_init(&dempty[b], 8);
+    }
+    mbar_init(bar_x, static_cast<uint32_t>(C));
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // every CTA's barriers are initialised before anyone arrives remotely
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && npanel > 0) {
+      const uint32_t bytes = P.nbp * 16384 + npanel * (P.rp * 128 + 16384);
+      mbar_arrive_expect_tx(bar_load, bytes);
+      const uint64_t keep = l2_policy_evict_last();
+      const uint64_t stream = l2_policy_evict_first();
+      for (int p = 0; p < P.nbp; ++p) tma_load_2d(sB + p * 16384, &batch.tm_b[pi], bar_load, p * 64, n0, keep);
+      for (int p = 0; p < npanel; ++p) {
+        tma_load_2d(sA + p * (P.rp * 128), &batch.tm_a[pi], bar_load, k_begin + p * 64, 0, keep);
+        tma_load_2d(sW + p * 16384, &batch.tm_w[pi], bar_load, k_begin + p * 64, n0, stream);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(128, 64, false, true);
+      if (npanel > 0 && mbar_wait(bar_load, 0, abort_flag, kSiteReqLoad)) {
+        tc_fence_after();
+        const uint32_t b_base = smem_u32(sB);
+        for (int p = 0; p < npanel; ++p) {
+          const int b = p & 1;
+          if (!mbar_wait(&dempty[b], ((p >> 1) & 1) ^ 1, abort_flag, kSiteReqDE)) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + p * (P.rp * 128));
+          for (int kk = 0; kk < P.rp / 16; ++kk) {
+            const uint64_t ad = make_sdesc(b_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+            const uint64_t bd = make_sdesc(a_base + kk * 2048, P.rp * 128, 1024, kLayoutSW128);
+            umma_f16(tmem + b * 64, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&dfull[b]);
+        }
+      }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, nullptr, kSiteReqFinal);
+    }
+  } else {
+    // ---------------- epilogue warps 2-9 ----------------
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;  // columns [32*half, 32*half + 32) of each panel
+    const int row = q * 32 + lane;
+    const int sw = row & 7;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + half * 32;
+    float pmax = 0.f;
+    bool nan = false;
+    bool bad = false;
+    for (int p = 0; p < npanel; ++p) {
+      const int b = p & 1;
+      const bool ok = mbar_wait(&dfull[b], (p >> 1) & 1, abort_flag, kSiteReqD);
+      if (named_bar_any(1, 256, !ok || *abort_flag)) {
+        bad = true;
+        break;
+      }
+      tc_fence_after();
+      uint32_t acc[32];
+      tmem_ld32(taddr + b * 64, acc);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dempty[b]);
+      uint8_t* wrow = sW + p * 16384 + row * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4* chunk = reinterpret_cast<uint4*>(wrow + (((4 * half + c) ^ sw) << 4));
+        uint4 w = *chunk;
+        uint32_t* wv = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __half2 d = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * P.s,
+                                              __uint_as_float(acc[8 * c + 2 * e + 1]) * P.s);
+          __half2 m = __hadd2(*reinterpret_cast<__half2*>(&wv[e]), d);
+          wv[e] = *reinterpret_cast<uint32_t*>(&m);
+          const float lo = __low2float(m), hi = __high2float(m);
+          nan |= (lo != lo) | (hi != hi);
+          pmax = fmaxf(pmax, fmaxf(fabsf(lo), fabsf(hi)));
+        }
+        *chunk = w;
+      }
+    }
+    // ---- row maximum across the two halves, then across the cluster.  Every
+    // CTA takes part even after an abort, so no peer waits on a missing push. ----
+    const bool bad_any = named_bar_any(1, 256, bad || *abort_flag);
+    red[half * 128 + row] = (nan || bad_any) ? __int_as_float(0x7fc00000) : pmax;
+    named_bar_sync(1, 256);
+    if (half == 0) {
+      const float a = red[row], c2 = red[128 + row];
+      const float mine = (a != a || c2 != c2) ? __int_as_float(0x7fc00000) : fmaxf(a, c2);
+      const uint32_t slot = smem_u32(&xred[rank * 128 + row]);
+      for (int d = 0; d < C; ++d) st_shared_cluster_f32(mapa_shared(slot, d), mine);
+    }
+    named_bar_sync(1, 256);
+    if (warp == 2 && lane == 0) {
+      fence_acq_rel_cluster();
+      for (int d = 0; d < C; ++d) mbar_arrive_remote(mapa_shared(smem_u32(bar_x), d));
+    }
+    const bool okx = mbar_wait_cluster(bar_x, 0, abort_flag, kSiteReqX);
+    if (!named_bar_any(1, 256, !okx || bad_any || *abort_flag)) {
+      {
+        float m = 0.f;
+        bool nn = false;
+        for (int d = 0; d < C; ++d) {
+          const float v = xred[d * 128 + row];
+          nn |= (v != v);
+          m = fmaxf(m, v);
+        }
+        const float scale = scale_from_amax<BW_DTYPE_F16>(m, nn);
+        const float rcp = __frcp_rn(scale);
+        if (rank == 0 && half == 0 && n0 + row < P.n) P.scale[n0 + row] = __float2half_rn(scale);
+        // ---- quantise the resident merged slice in place, one 64-column panel at a time ----
+        for (int p = 0; p < npanel; ++p) {
+          uint8_t* panel = sW + p * 16384;
+          uint4 v[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            v[c] = *reinterpret_cast<const uint4*>(panel + row * 128 + (((4 * half + c) ^ sw) << 4));
+          named_bar_sync(1, 256);  // every merged value of the panel is in registers before it is overwritten
+          int8_t qv[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t* hv = reinterpret_cast<const uint32_t*>(&v[c]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __half2 h = *reinterpret_cast<const __half2*>(&hv[e]);
+              qv[8 * c + 2 * e] = quant_fast<BW_DTYPE_F16>(__low2float(h), scale, rcp);
+              qv[8 * c + 2 * e + 1] = quant_fast<BW_DTYPE_F16>(__high2float(h), scale, rcp);
+            }
+          }
+          // int8 panel [128 rows x 64 B], 64-byte swizzle: chunk c of row r at c ^ ((r >> 1) & 3)
+          const int swz = (row >> 1) & 3;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            *reinterpret_cast<uint4*>(panel + row * 64 + (((2 * half + c) ^ swz) << 4)) =
+                *reinterpret_cast<const uint4*>(&qv[16 * c]);
+          fence_proxy_async_smem();
+          named_bar_sync(1, 256);
+          if (warp == 2 && lane == 0 && k_begin + p * 64 < P.k) {
+            tma_store_2d(&batch.tm_q[pi], panel, k_begin + p * 64, n0);
+            tma_store_commit();
+          }
+        }
+        if (warp == 2 && lane == 0) tma_store_wait0();
+      }
+    }
+  }
+
+  tc_fence_before();
+  // All DSMEM traffic of the cluster is finished before any CTA exits; every
+  // wait above is bounded, so every thread of every CTA reaches this point.
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // CUDA-core kernels: add_delta_ and the fallbacks for shapes TMA cannot address
 // ---------------------------------------------------------------------------
 __global__ void add_delta_kernel(__half* __restrict__ w, const __half* __restrict__ d, int64_t numel, int vec) {
@@ -428,6 +680,102 @@ static int check_lora_args(const char* op, const void* a, const void* b, int64_t
   return BW_OK;
 }
 
+// ---- grouped cluster requant: host side ----
+static bool req_cluster_eligible(const bw_lora_requant_problem& P) {
+  const auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  return lora_tc_ok(P.a, P.b, P.k, P.r) && al16(P.w) && al16(P.q) && (P.ldw * 2) % 16 == 0 && P.ldq % 16 == 0 &&
+         P.k <= 4096 && P.n >= 1 && P.k >= 1;
+}
+
+static int launch_req_cluster(const bw_lora_requant_problem* probs, const int* idx, int count, int cluster,
+                              cudaStream_t st) {
+  ReqBatch b;
+  memset(&b, 0, sizeof(b));
+  b.count = count;
+  b.cluster = cluster;
+  int rp_max = 16, nbp_max = 1, np_max = 1, rb = 0;
+  for (int j = 0; j < count; ++j) {
+    const bw_lora_requant_problem& P = probs[idx[j]];
+    ReqProblem& R = b.p[j];
+    R.scale = static_cast<__half*>(P.scale);
+    R.s = P.scaling;
+    R.n = static_cast<int>(P.n);
+    R.k = static_cast<int>(P.k);
+    R.r = static_cast<int>(P.r);
+    R.rp = (R.r + 15) / 16 * 16;
+    R.nbp = (R.rp + 63) / 64;
+    R.kc = ((R.k + cluster - 1) / cluster + 63) / 64 * 64;
+    R.rb0 = rb;
+    rb += (R.n + 127) / 128;
+    rp_max = std::max(rp_max, R.rp);
+    nbp_max = std::max(nbp_max, R.nbp);
+    np_max = std::max(np_max, R.kc / 64);
+    if (int e = make_tmap_2d(&b.tm_w[j], P.w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, P.n, P.k, P.ldw * 2, 128, 64,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
+    if (int e = make_tmap_2d(&b.tm_a[j], P.a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, P.r, P.k, P.k * 2, R.rp, 64,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
+    if (int e = make_tmap_2d(&b.tm_b[j], P.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, P.n, P.r, P.r * 2, 128, 64,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
+    if (int e = make_tmap_2d(&b.tm_q[j], P.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, P.n, P.k, P.ldq, 128, 64,
+                             CU_TENSOR_MAP_SWIZZLE_64B))
+      return e;
+  }
+  b.total_rb = rb;
+  b.off_a = nbp_max * 16384;
+  b.off_w = b.off_a + (np_max * rp_max * 128 + 1023) / 1024 * 1024;
+  b.off_red = b.off_w + np_max * 16384;
+  b.off_bar = b.off_red + (256 + kReqMaxCluster * 128) * 4;
+  const int smem = b.off_bar + 128 + 1024;
+  if (smem > 232448) return fail(BW_ERR_UNSUPPORTED, "lora_merge_requant: shared memory plan of %d bytes", smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster, rb);
+  cfg.blockDim = dim3(kReqThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, lora_requant_cluster_kernel, b),
+                    "cudaLaunchKernelEx(lora_requant_cluster_kernel)");
+}
+
+// Largest cluster size (16, else 8) the device can co-schedule for this kernel.
+static int req_cluster_size() {
+  static int cached[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev & 63]) return cached[dev & 63];
+  cudaFuncSetAttribute(lora_requant_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 2048);
+  cudaFuncSetAttribute(lora_requant_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  int size = 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(16, 1);
+  cfg.blockDim = dim3(kReqThreads);
+  cfg.dynamicSmemBytes = 140 * 1024;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 16;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, lora_requant_cluster_kernel, &cfg) == cudaSuccess && clusters > 0)
+    size = 16;
+  cudaGetLastError();
+  cached[dev & 63] = size;
+  return size;
+}
+
 }  // namespace bw
 
 extern "C" int bw_add_delta(void* w, const void* delta, int64_t numel, void* stream) {
@@ -494,16 +842,13 @@ extern "C" int bw_lora_merge(const void* w, int64_t ldw, const void* a, const vo
   return launch_lora_tc<kModeMerge>(tb, ta, tw, to, nullptr, (int)n, (int)k, (int)r, scaling, st);
 }
 
-extern "C" int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, const void* b, float scaling, int8_t* q,
-                                     int64_t ldq, void* scale, int64_t n, int64_t k, int64_t r, void* stream) {
-  using namespace bw;
-  if (int s = check_lora_args("lora_merge_requant", a, b, n, k, r)) return s;
-  if (k < 1) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: k must be >= 1");
-  if (n == 0) return BW_OK;
-  if (!w || !q || !scale) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: null pointer");
-  if (ldw < k || ldq < k) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: row stride smaller than k");
-  if (int s = require_sm100()) return s;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+namespace bw {
+// One problem through the two-pass cluster kernel (any K) or, for layouts TMA
+// cannot address, the CUDA-core kernel.
+static int merge_requant_single(const bw_lora_requant_problem& Pr, cudaStream_t st) {
+  const void* w = Pr.w; const int64_t ldw = Pr.ldw; const void* a = Pr.a; const void* b = Pr.b;
+  const float scaling = Pr.scaling; int8_t* q = Pr.q; const int64_t ldq = Pr.ldq; void* scale = Pr.scale;
+  const int64_t n = Pr.n, k = Pr.k, r = Pr.r;
   const bool aligned = reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
                        (ldw * 2) % 16 == 0 && ldq % 16 == 0;
   if (!lora_tc_ok(a, b, k, r) || !aligned) {
@@ -519,4 +864,58 @@ extern "C" int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, 
   if (int s = make_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k, ldq, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
   return launch_lora_tc<kModeRequant>(tb, ta, tw, tq, static_cast<__half*>(scale), (int)n, (int)k, (int)r, scaling, st);
+}
+}  // namespace bw
+
+extern "C" int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int count, void* stream) {
+  using namespace bw;
+  if (count < 0 || (count > 0 && problems == nullptr))
+    return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: bad problem list");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<int> grouped;
+  for (int i = 0; i < count; ++i) {
+    const bw_lora_requant_problem& P = problems[i];
+    if (int e = check_lora_args("lora_merge_requant", P.a, P.b, P.n, P.k, P.r)) return e;
+    if (P.k < 1) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: k must be >= 1 (problem %d)", i);
+    if (P.n == 0) continue;
+    if (!P.w || !P.q || !P.scale) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: null pointer (problem %d)", i);
+    if (P.ldw < P.k || P.ldq < P.k)
+      return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: row stride smaller than k (problem %d)", i);
+  }
+  if (int e = require_sm100()) return e;
+  const int cluster = req_cluster_size();
+  for (int i = 0; i < count; ++i) {
+    const bw_lora_requant_problem& P = problems[i];
+    if (P.n == 0) continue;
+    if (req_cluster_eligible(P) && P.k <= static_cast<int64_t>(cluster) * 256) {
+      grouped.push_back(i);
+    } else if (int e = merge_requant_single(P, st)) {
+      return e;
+    }
+  }
+  for (size_t j = 0; j < grouped.size(); j += kReqMaxProblems) {
+    const int c = static_cast<int>(std::min<size_t>(kReqMaxProblems, grouped.size() - j));
+    int64_t kmax = 1;
+    for (int t = 0; t < c; ++t) kmax = std::max(kmax, problems[grouped[j + t]].k);
+    const int csize = static_cast<int>(std::min<int64_t>(cluster, (kmax + 127) / 128));
+    if (int e = launch_req_cluster(problems, grouped.data() + j, c, csize < 1 ? 1 : csize, st)) return e;
+  }
+  return BW_OK;
+}
+
+extern "C" int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, const void* b, float scaling, int8_t* q,
+                                     int64_t ldq, void* scale, int64_t n, int64_t k, int64_t r, void* stream) {
+  bw_lora_requant_problem P;
+  P.w = w;
+  P.ldw = ldw;
+  P.a = a;
+  P.b = b;
+  P.scaling = scaling;
+  P.q = q;
+  P.ldq = ldq;
+  P.scale = scale;
+  P.n = n;
+  P.k = k;
+  P.r = r;
+  return bw_lora_merge_requant_batched(&P, 1, stream);
 }

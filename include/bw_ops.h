@@ -130,6 +130,26 @@ int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, const void*
                           void* stream);
 
 /*
+ * Batched fused merge + requantisation: every problem is
+ * (q, scale) = quantize_weight_int8(add_delta(w, lora_delta(a, b, scaling))),
+ * e.g. all projections an adapter touches, in as few launches as possible
+ * (one per 16 problems with K <= 4096; other shapes run one at a time).
+ * Same per-problem contract as bw_lora_merge_requant; no scratch memory.
+ */
+typedef struct bw_lora_requant_problem {
+  const void* w;   /* [n, k] fp16, row stride ldw */
+  int64_t ldw;
+  const void* a;   /* [r, k] fp16 contiguous */
+  const void* b;   /* [n, r] fp16 contiguous */
+  float scaling;
+  int8_t* q;       /* [n, k] int8, row stride ldq */
+  int64_t ldq;
+  void* scale;     /* [n] fp16 */
+  int64_t n, k, r;
+} bw_lora_requant_problem;
+int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int count, void* stream);
+
+/*
  * Device-side status of the current device: BW_OK, or BW_ERR_DEVICE_TIMEOUT
  * if a kernel's bounded wait expired since the last clear.  Synchronises
  * `stream`.  If `detail` is non-NULL it receives the failing wait site id.

@@ -152,3 +152,20 @@ def test_lora_full_size_70b_requant_properties(cuda_dev, ops):
     err = (merged.double() - ref).abs()
     # one fp16 rounding of the delta and one of the sum
     assert bool((err <= (ref.abs() + d.abs()) * 2.0 ** -10 + 2.0 ** -24).all())
+
+
+def test_lora_merge_requant_batched_equals_single(cuda_dev, ops):
+    """One batched launch over mixed shapes/ranks gives the single-problem results bit for bit."""
+    cuda, _ = ops
+    specs = [(16, 2048, 1024), (16, 1024, 1024), (128, 1024, 2048), (64, 3072, 1024), (16, 1024, 3072),
+             (128, 130, 1000), (8, 1, 64), (32, 257, 4096), (16, 96, 5000), (12, 40, 72)]
+    items = []
+    for i, (r, n, k) in enumerate(specs):
+        A, B, W = make(600 + i, r, n, k)
+        items.append((dev16(W, cuda_dev), dev16(A, cuda_dev), dev16(B, cuda_dev), 2.0 if i % 3 else 0.75))
+    outs = cuda.lora_merge_requant_batched(items)
+    for (W, A, B, s), (q, sc) in zip(items, outs):
+        q1, s1 = cuda.lora_merge_requant(W, A, B, s)
+        assert torch.equal(q, q1) and torch.equal(sc, s1)
+        qm, sm = quant.quantize_weight_int8(cuda.lora_merge(W, A, B, s).cpu().numpy(), F16)
+        assert np.array_equal(q.cpu().numpy(), qm) and np.array_equal(sc.cpu().numpy(), sm)
