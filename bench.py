@@ -154,7 +154,7 @@ class MergeRequantWorkload:
     """cfg2: LoRA delta + merge + requant for one Qwen3-0.6B layer, r in {16, 128}, per step."""
 
     name = "cfg2"
-    kernel = "lora_requant_cluster_kernel"
+    kernel = "lora_requant_coop_kernel"
     unit = "TFLOPS"
     metric_kind = "tflops"
     ranks_r = (16, 128)
@@ -192,6 +192,9 @@ class MergeRequantWorkload:
                                    self.S[li][r][p].data_ptr(), n, k, r) for p, (_, k, n) in enumerate(QWEN)])
                 per_r[r] = arr
             self.problems.append(per_r)
+        need = max(self.lib.bw_lora_merge_requant_batched_workspace_size(a, len(QWEN))
+                   for per_r in self.problems for a in per_r.values())
+        self.ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
         self.launches_per_step = len(self.ranks_r)
 
     def config(self):
@@ -202,7 +205,8 @@ class MergeRequantWorkload:
     def step(self, s, st, events=None):
         li = s % self.layers
         for r in self.ranks_r:
-            rc = self.lib.bw_lora_merge_requant_batched(self.problems[li][r], len(QWEN), st)
+            rc = self.lib.bw_lora_merge_requant_batched(self.problems[li][r], len(QWEN), self.ws.data_ptr(),
+                                                        self.ws.numel(), st)
             if rc:
                 raise RuntimeError(self.lib.bw_last_error().decode())
 

@@ -52,8 +52,11 @@ SIGNATURES = {
     "bw_lora_delta": (_c.c_int, [_P, _P, _P, _I64, _I64, _I64, _c.c_float, _P]),
     "bw_add_delta": (_c.c_int, [_P, _P, _I64, _P]),
     "bw_lora_merge": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),
-    "bw_lora_merge_requant": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _P, _I64, _I64, _I64, _P]),
-    "bw_lora_merge_requant_batched": (_c.c_int, [_c.POINTER(RequantProblem), _c.c_int, _P]),
+    "bw_lora_merge_requant_workspace_size": (_c.c_size_t, [_I64, _I64, _I64]),
+    "bw_lora_merge_requant": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _P, _I64, _I64, _I64, _P,
+                                         _c.c_size_t, _P]),
+    "bw_lora_merge_requant_batched_workspace_size": (_c.c_size_t, [_c.POINTER(RequantProblem), _c.c_int]),
+    "bw_lora_merge_requant_batched": (_c.c_int, [_c.POINTER(RequantProblem), _c.c_int, _P, _c.c_size_t, _P]),
     "bw_device_status": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_int), _P]),
 }
 

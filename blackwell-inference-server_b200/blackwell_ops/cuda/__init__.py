@@ -25,6 +25,20 @@ import torch
 
 from .._lib import RequantProblem, check, lib, stream_ptr
 
+_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Requantisation scratch (panel maxima + grid counter) per (device, stream); no initialisation needed."""
+    if nbytes == 0:
+        return None
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr(device))
+    ws = _ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws[key] = ws
+    return ws
+
 
 def _check_ab(A: torch.Tensor, B: torch.Tensor) -> tuple[int, int, int]:
     if not (A.is_cuda and B.is_cuda):
@@ -127,9 +141,12 @@ def lora_merge_requant(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
         from ..kernels import quantize_weight_int8
 
         return quantize_weight_int8(W)
+    nbytes = lib.bw_lora_merge_requant_workspace_size(N, K, r)
+    ws = _workspace(W.device, nbytes)
     with torch.cuda.device(W.device):
         check(lib.bw_lora_merge_requant(W.data_ptr(), W.stride(0), A.data_ptr(), B.data_ptr(), float(scaling),
-                                        q.data_ptr(), K, scale.data_ptr(), N, K, r, stream_ptr(W.device)),
+                                        q.data_ptr(), K, scale.data_ptr(), N, K, r,
+                                        ws.data_ptr() if ws is not None else None, nbytes, stream_ptr(W.device)),
               "lora_merge_requant")
     return q, scale
 
@@ -173,8 +190,11 @@ def lora_merge_requant_batched(items):
                                     q.data_ptr(), K, sc.data_ptr(), N, K, r))
     if probs:
         arr = (RequantProblem * len(probs))(*probs)
+        nbytes = lib.bw_lora_merge_requant_batched_workspace_size(arr, len(probs))
+        ws = _workspace(dev, nbytes)
         with torch.cuda.device(dev):
-            check(lib.bw_lora_merge_requant_batched(arr, len(probs), stream_ptr(dev)), "lora_merge_requant_batched")
+            check(lib.bw_lora_merge_requant_batched(arr, len(probs), ws.data_ptr() if ws is not None else None,
+                                                    nbytes, stream_ptr(dev)), "lora_merge_requant_batched")
     return outs
 
 

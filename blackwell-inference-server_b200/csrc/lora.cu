@@ -285,32 +285,35 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
-// Grouped merge + requantisation, one cluster per 128-row block (K <= 4096).
+// Grouped, cooperative merge + requantisation.
 //
 // One launch covers up to kReqMaxProblems projections (e.g. every projection an
-// adapter touches).  A cluster of C CTAs (C <= 16) owns one 128-row block of one
-// problem; CTA c owns columns [c*Kc, (c+1)*Kc), Kc <= 256, and:
-//   1. TMA-loads B[128 rows, r], its A[r, Kc] slice and its W[128, Kc] slice
-//      once (W is read from HBM exactly once);
-//   2. per 64-column panel: tcgen05.mma (M=128, N=64, K=16 x r/16) into one of
-//      two TMEM accumulators; 8 epilogue warps merge W' = fp16(W + fp16(acc*s))
-//      IN PLACE in shared memory (__hadd2 is the correctly rounded fp16 sum,
-//      which equals fp16(fp32(W) + fp32(delta)) for fp16 operands) and track
-//      the row's |W'| maximum;
-//   3. push the per-row maxima to every CTA of the cluster through distributed
-//      shared memory (bounded mbarrier wait), reduce, derive the scale;
-//   4. quantise the resident merged slice in place (fast exact quantiser) and
-//      TMA-store int8 panels (64-byte swizzle).
-// The merged weight never leaves the SM; no scratch memory.
+// adapter touches).  The work is cut into uniform items, one 128-row x 64-column
+// panel each, numbered problem-major then row block then panel, and dealt to a
+// grid of co-resident CTAs in contiguous ranges (cooperative launch).  Each CTA
+// walks its range twice:
+//   pass 1: TMA brings the W panel and the A[r, 64] panel (and B[128, r] when
+//           the row block changes, double-buffered); tcgen05.mma (M=128, N=64,
+//           K=16 x r/16) -> TMEM; 8 epilogue warps merge
+//           W' = fp16(W + fp16(acc*s)) in registers (__hadd2 is the correctly
+//           rounded fp16 sum = fp16(fp32(W) + fp32(delta))) and write each
+//           row's |W'| maximum of the panel half to the workspace;
+//   grid barrier (bounded spin on a workspace counter; every CTA is resident);
+//   pass 2: the same panels again (W hits L2, ΔW recomputed on the tensor
+//           core), row scale from the panel maxima, packed exact quantiser,
+//           int8 stored by each warp with its own TMA store (no CTA barrier).
+// The producer and MMA run ahead into pass 2 while the epilogue waits at the
+// grid barrier, so the weight stream does not stall.  The merged weight never
+// touches memory; the workspace holds 2 floats per row per panel + a counter.
 // ---------------------------------------------------------------------------
 constexpr int kReqMaxProblems = 16;
-constexpr int kReqMaxCluster = 16;
 constexpr int kReqThreads = 320;  // warp 0 TMA, warp 1 MMA/TMEM, warps 2-9 epilogue
+constexpr int kReqStages = 3;
 
 struct ReqProblem {
   __half* scale;
   float s;
-  int n, k, r, rp, nbp, kc, rb0;  // rp: r rounded to 16; kc: columns per CTA; rb0: first row block
+  int n, k, r, rp, nbp, npanel, rb, item0;  // rp: r rounded to 16; item0: first item of this problem
 };
 
 struct ReqBatch {
@@ -320,52 +323,77 @@ struct ReqBatch {
   CUtensorMap tm_q[kReqMaxProblems];
   ReqProblem p[kReqMaxProblems];
   int count;
-  int total_rb;
-  int cluster;
-  // shared-memory carve-up (bytes, 1024-aligned), sized for the largest problem
-  int off_a, off_w, off_red, off_bar;
+  int total_items;
+  float* maxima;   // [total_items][2][128]
+  int* counter;    // grid barrier, zeroed before the launch
+  int b_bytes;     // one B buffer (nbp_max * 16 KB)
+  int stage_bytes; // 16 KB W panel + rp_max*128 B A panel, rounded to 1 KB
+  int off_ring, off_q, off_bar;
 };
 
-enum ReqWaitSite : int { kSiteReqLoad = 211, kSiteReqD = 212, kSiteReqDE = 213, kSiteReqX = 214, kSiteReqFinal = 215 };
+enum ReqWaitSite : int {
+  kSiteReqB = 211,
+  kSiteReqEmpty = 212,
+  kSiteReqFull = 213,
+  kSiteReqD = 214,
+  kSiteReqDE = 215,
+  kSiteReqGrid = 216,
+  kSiteReqFinal = 217,
+  kSiteReqBEmpty = 218,
+};
 
-__global__ void __launch_bounds__(kReqThreads, 1) lora_requant_cluster_kernel(const __grid_constant__ ReqBatch batch) {
+struct ReqItem {
+  int pi, rb, panel;
+};
+
+__device__ __forceinline__ ReqItem req_item(const ReqBatch& bt, int item) {
+  int pi = 0;
+  while (pi + 1 < bt.count && bt.p[pi + 1].item0 <= item) ++pi;
+  const int local = item - bt.p[pi].item0;
+  ReqItem r;
+  r.pi = pi;
+  r.rb = local / bt.p[pi].npanel;
+  r.panel = local % bt.p[pi].npanel;
+  return r;
+}
+
+__global__ void __launch_bounds__(kReqThreads, 2) lora_requant_coop_kernel(const __grid_constant__ ReqBatch batch) {
+  constexpr int S = kReqStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sB = smem;
-  uint8_t* sA = smem + batch.off_a;
-  uint8_t* sW = smem + batch.off_w;
-  float* red = reinterpret_cast<float*>(smem + batch.off_red);  // [2][128] per-half maxima
-  float* xred = red + 256;                                       // [C][128] cluster maxima
-  uint64_t* bar_load = reinterpret_cast<uint64_t*>(smem + batch.off_bar);
-  uint64_t* dfull = bar_load + 1;    // 2
+  uint8_t* sB = smem;                                  // 2 x b_bytes
+  uint8_t* sRing = smem + batch.off_ring;              // S x stage_bytes
+  uint8_t* sQ = smem + batch.off_q;                    // 8 warps x 2 x 1 KB int8 staging
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(smem + batch.off_bar);  // 2
+  uint64_t* bempty = bfull + 2;      // 2
+  uint64_t* full = bempty + 2;       // S
+  uint64_t* empty = full + S;        // S
+  uint64_t* dfull = empty + S;       // 2
   uint64_t* dempty = dfull + 2;      // 2
-  uint64_t* bar_x = dempty + 2;
-  uint64_t* final_bar = bar_x + 1;
+  uint64_t* final_bar = dempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int C = static_cast<int>(gridDim.x);
-  const int rank = static_cast<int>(cluster_ctarank());
-
-  // which problem / row block this cluster owns
-  const int rb_global = blockIdx.y;
-  int pi = 0;
-  while (pi + 1 < batch.count && batch.p[pi + 1].rb0 <= rb_global) ++pi;
-  const ReqProblem& P = batch.p[pi];
-  const int n0 = (rb_global - P.rb0) * 128;
-  const int k_begin = rank * P.kc;
-  const int k_len = max(0, min(P.kc, P.k - k_begin));
-  const int npanel = (k_len + 63) / 64;
+  const int G = static_cast<int>(gridDim.x);
+  const int T = batch.total_items;
+  const int lo = static_cast<int>((static_cast<long long>(T) * blockIdx.x) / G);
+  const int hi = static_cast<int>((static_cast<long long>(T) * (blockIdx.x + 1)) / G);
+  const int nmine = hi - lo;
+  const int steps = 2 * nmine;  // pass 1 items, then pass 2 items
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_load, 1);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&bfull[b], 1);
+      mbar_init(&bempty[b], 1);
       mbar_init(&dfull[b], 1);
       mbar_init(&dempty[b], 8);
     }
-    mbar_init(bar_x, static_cast<uint32_t>(C));
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1 + 8);  // MMA commit + 8 epilogue warps
+    }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -375,42 +403,77 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_cluster_kernel(co
     tmem_relinquish();
   }
   tc_fence_before();
-  cluster_sync_all();  // every CTA's barriers are initialised before anyone arrives remotely
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // B buffer use: a new buffer whenever (problem, row block) changes along the walk;
+  // the walk repeats identically in pass 2.
   if (warp == 0) {
-    if (lane == 0 && npanel > 0) {
-      const uint32_t bytes = P.nbp * 16384 + npanel * (P.rp * 128 + 16384);
-      mbar_arrive_expect_tx(bar_load, bytes);
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
-      const uint64_t stream = l2_policy_evict_first();
-      for (int p = 0; p < P.nbp; ++p) tma_load_2d(sB + p * 16384, &batch.tm_b[pi], bar_load, p * 64, n0, keep);
-      for (int p = 0; p < npanel; ++p) {
-        tma_load_2d(sA + p * (P.rp * 128), &batch.tm_a[pi], bar_load, k_begin + p * 64, 0, keep);
-        tma_load_2d(sW + p * 16384, &batch.tm_w[pi], bar_load, k_begin + p * 64, n0, stream);
+      int prev_key = -1, bseq = -1;
+      for (int it = 0; it < steps; ++it) {
+        const int item = lo + (it % nmine);
+        const ReqItem I = req_item(batch, item);
+        const ReqProblem& P = batch.p[I.pi];
+        const int key = item - I.panel;  // first item of the row block: identifies (problem, row block)
+        if (key != prev_key || it == nmine) {
+          prev_key = key;
+          ++bseq;
+          const int bb = bseq & 1;
+          // the buffer's previous row block must be finished by the MMA
+          if (!mbar_wait(&bempty[bb], ((bseq >> 1) & 1) ^ 1, abort_flag, kSiteReqBEmpty)) break;
+          mbar_arrive_expect_tx(&bfull[bb], P.nbp * 16384);
+          for (int p = 0; p < P.nbp; ++p)
+            tma_load_2d(sB + bb * batch.b_bytes + p * 16384, &batch.tm_b[I.pi], &bfull[bb], p * 64, I.rb * 128, keep);
+        }
+        const int st = it % S;
+        if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1, abort_flag, kSiteReqEmpty)) break;
+        uint8_t* slot = sRing + st * batch.stage_bytes;
+        mbar_arrive_expect_tx(&full[st], 16384 + P.rp * 128);
+        const int kx = I.panel * 64;
+        tma_load_2d(slot, &batch.tm_w[I.pi], &full[st], kx, I.rb * 128, it < nmine ? keep : l2_policy_evict_first());
+        tma_load_2d(slot + 16384, &batch.tm_a[I.pi], &full[st], kx, 0, keep);
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(128, 64, false, true);
-      if (npanel > 0 && mbar_wait(bar_load, 0, abort_flag, kSiteReqLoad)) {
-        tc_fence_after();
-        const uint32_t b_base = smem_u32(sB);
-        for (int p = 0; p < npanel; ++p) {
-          const int b = p & 1;
-          if (!mbar_wait(&dempty[b], ((p >> 1) & 1) ^ 1, abort_flag, kSiteReqDE)) break;
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + p * (P.rp * 128));
-          for (int kk = 0; kk < P.rp / 16; ++kk) {
-            const uint64_t ad = make_sdesc(b_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-            const uint64_t bd = make_sdesc(a_base + kk * 2048, P.rp * 128, 1024, kLayoutSW128);
-            umma_f16(tmem + b * 64, ad, bd, idesc, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&dfull[b]);
+      int prev_key = -1, bseq = -1;
+      bool ok = true;
+      for (int it = 0; it < steps && ok; ++it) {
+        const int item = lo + (it % nmine);
+        const ReqItem I = req_item(batch, item);
+        const ReqProblem& P = batch.p[I.pi];
+        const int key = item - I.panel;
+        if (key != prev_key || it == nmine) {
+          if (bseq >= 0) umma_commit(&bempty[bseq & 1]);  // previous row block's MMAs release its B buffer
+          prev_key = key;
+          ++bseq;
+          if (!mbar_wait(&bfull[bseq & 1], (bseq >> 1) & 1, abort_flag, kSiteReqB)) break;
         }
+        const int st = it % S;
+        const int d = it & 1;
+        if (!mbar_wait(&full[st], (it / S) & 1, abort_flag, kSiteReqFull) ||
+            !mbar_wait(&dempty[d], ((it >> 1) & 1) ^ 1, abort_flag, kSiteReqDE)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t b_base = smem_u32(sB + (bseq & 1) * batch.b_bytes);
+        const uint32_t a_base = smem_u32(sRing + st * batch.stage_bytes + 16384);
+        for (int kk = 0; kk < P.rp / 16; ++kk) {
+          const uint64_t ad = make_sdesc(b_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          const uint64_t bd = make_sdesc(a_base + kk * 2048, P.rp * 128, 1024, kLayoutSW128);
+          umma_f16(tmem + d * 64, ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&dfull[d]);
+        umma_commit(&empty[st]);
       }
-      umma_commit(final_bar);
+      umma_commit(final_bar);  // every issued MMA has completed before TMEM is freed
       mbar_wait(final_bar, 0, nullptr, kSiteReqFinal);
     }
   } else {
@@ -420,112 +483,149 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_cluster_kernel(co
     const int row = q * 32 + lane;
     const int sw = row & 7;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + half * 32;
-    float pmax = 0.f;
-    bool nan = false;
+    uint8_t* stage_q = sQ + (warp - 2) * 2048;  // this warp's two 1 KB staging buffers
     bool bad = false;
-    for (int p = 0; p < npanel; ++p) {
-      const int b = p & 1;
-      const bool ok = mbar_wait(&dfull[b], (p >> 1) & 1, abort_flag, kSiteReqD);
-      if (named_bar_any(1, 256, !ok || *abort_flag)) {
+    int qbuf = 0;
+    int cur_key = -1;
+    float scale = 0.f, rcp = 0.f;
+    bool fast_row = false;
+    for (int it = 0; it < steps; ++it) {
+      if (it == nmine) {
+        // ---- grid barrier: every CTA's pass-1 maxima are in the workspace ----
+        __threadfence();
+        if (named_bar_any(1, 256, bad || *abort_flag)) bad = true;
+        // only the spinning thread knows the outcome: it alone votes, the OR spreads it
+        bool grid_failed = false;
+        if (warp == 2 && lane == 0) {
+          atomicAdd(batch.counter, 1);
+          const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
+          const long long t0 = clock64();
+          while (atomicAdd(batch.counter, 0) < G) {
+            if (clock64() - t0 > limit) {
+              record_timeout(kSiteReqGrid);
+              grid_failed = true;
+              *abort_flag = 1;
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+        if (named_bar_any(1, 256, grid_failed)) bad = true;
+        __threadfence();
+      }
+      if (bad) continue;  // keep walking so every barrier above is reached the same number of times
+      const int item = lo + (it % nmine);
+      const ReqItem I = req_item(batch, item);
+      const ReqProblem& P = batch.p[I.pi];
+      const bool pass2 = it >= nmine;
+      const int st = it % S;
+      const int d = it & 1;
+      const bool ok = mbar_wait(&dfull[d], (it >> 1) & 1, abort_flag, kSiteReqD) &&
+                      mbar_wait(&full[st], (it / S) & 1, abort_flag, kSiteReqFull);
+      if (!ok) {
         bad = true;
-        break;
+        continue;
       }
       tc_fence_after();
       uint32_t acc[32];
-      tmem_ld32(taddr + b * 64, acc);
+      tmem_ld32(taddr + d * 64, acc);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dempty[b]);
-      uint8_t* wrow = sW + p * 16384 + row * 128;
+      if (lane == 0) mbar_arrive(&dempty[d]);
+      const uint8_t* wrow = sRing + st * batch.stage_bytes + row * 128;
+      uint4 wv[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) wv[c] = *reinterpret_cast<const uint4*>(wrow + (((4 * half + c) ^ sw) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+      __half2 merged[16];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint4* chunk = reinterpret_cast<uint4*>(wrow + (((4 * half + c) ^ sw) << 4));
-        uint4 w = *chunk;
-        uint32_t* wv = reinterpret_cast<uint32_t*>(&w);
+        const uint32_t* w32 = reinterpret_cast<const uint32_t*>(&wv[c]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const __half2 d = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * P.s,
-                                              __uint_as_float(acc[8 * c + 2 * e + 1]) * P.s);
-          __half2 m = __hadd2(*reinterpret_cast<__half2*>(&wv[e]), d);
-          wv[e] = *reinterpret_cast<uint32_t*>(&m);
-          const float lo = __low2float(m), hi = __high2float(m);
-          nan |= (lo != lo) | (hi != hi);
-          pmax = fmaxf(pmax, fmaxf(fabsf(lo), fabsf(hi)));
+          const __half2 dl = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * P.s,
+                                               __uint_as_float(acc[8 * c + 2 * e + 1]) * P.s);
+          merged[4 * c + e] = __hadd2(*reinterpret_cast<const __half2*>(&w32[e]), dl);
         }
-        *chunk = w;
       }
-    }
-    // ---- row maximum across the two halves, then across the cluster.  Every
-    // CTA takes part even after an abort, so no peer waits on a missing push. ----
-    const bool bad_any = named_bar_any(1, 256, bad || *abort_flag);
-    red[half * 128 + row] = (nan || bad_any) ? __int_as_float(0x7fc00000) : pmax;
-    named_bar_sync(1, 256);
-    if (half == 0) {
-      const float a = red[row], c2 = red[128 + row];
-      const float mine = (a != a || c2 != c2) ? __int_as_float(0x7fc00000) : fmaxf(a, c2);
-      const uint32_t slot = smem_u32(&xred[rank * 128 + row]);
-      for (int d = 0; d < C; ++d) st_shared_cluster_f32(mapa_shared(slot, d), mine);
-    }
-    named_bar_sync(1, 256);
-    if (warp == 2 && lane == 0) {
-      fence_acq_rel_cluster();
-      for (int d = 0; d < C; ++d) mbar_arrive_remote(mapa_shared(smem_u32(bar_x), d));
-    }
-    const bool okx = mbar_wait_cluster(bar_x, 0, abort_flag, kSiteReqX);
-    if (!named_bar_any(1, 256, !okx || bad_any || *abort_flag)) {
-      {
-        float m = 0.f;
-        bool nn = false;
-        for (int d = 0; d < C; ++d) {
-          const float v = xred[d * 128 + row];
-          nn |= (v != v);
-          m = fmaxf(m, v);
+      const int n = I.rb * 128 + row;
+      if (!pass2) {
+        __half2 hm = __float2half2_rn(0.0f);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) hm = __hmax2_nan(hm, __habs2(merged[e]));
+        const float l = __low2float(hm), h = __high2float(hm);
+        batch.maxima[(static_cast<size_t>(item) * 2 + half) * 128 + row] =
+            (l != l || h != h) ? __int_as_float(0x7fc00000) : fmaxf(l, h);
+      } else {
+        const int key = item - I.panel;
+        if (key != cur_key) {
+          // scale of this row from every panel's maxima of the row block
+          cur_key = key;
+          float m = 0.f;
+          bool nn = false;
+          const float* mx = batch.maxima + static_cast<size_t>(key) * 2 * 128 + row;
+          for (int j = 0; j < 2 * P.npanel; ++j) {
+            const float v = __ldcg(mx + j * 128);
+            nn |= (v != v);
+            m = fmaxf(m, v);
+          }
+          scale = scale_from_amax<BW_DTYPE_F16>(m, nn);
+          rcp = __frcp_rn(scale);
+          fast_row = scale > 0.0f && rcp < 1.0e30f;  // finite, non-zero scale: every quotient is finite
         }
-        const float scale = scale_from_amax<BW_DTYPE_F16>(m, nn);
-        const float rcp = __frcp_rn(scale);
-        if (rank == 0 && half == 0 && n0 + row < P.n) P.scale[n0 + row] = __float2half_rn(scale);
-        // ---- quantise the resident merged slice in place, one 64-column panel at a time ----
-        for (int p = 0; p < npanel; ++p) {
-          uint8_t* panel = sW + p * 16384;
-          uint4 v[4];
+        if (I.panel == 0 && half == 0 && n < P.n) P.scale[n] = __float2half_rn(scale);
+        uint32_t qw[8];
+        if (fast_row) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            v[c] = *reinterpret_cast<const uint4*>(panel + row * 128 + (((4 * half + c) ^ sw) << 4));
-          named_bar_sync(1, 256);  // every merged value of the panel is in registers before it is overwritten
-          int8_t qv[32];
+          for (int e = 0; e < 8; ++e) qw[e] = quant4_f16(merged[2 * e], merged[2 * e + 1], scale, rcp);
+        } else {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t* hv = reinterpret_cast<const uint32_t*>(&v[c]);
+          for (int e = 0; e < 8; ++e) {
+            uint32_t v = 0;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __half2 h = *reinterpret_cast<const __half2*>(&hv[e]);
-              qv[8 * c + 2 * e] = quant_fast<BW_DTYPE_F16>(__low2float(h), scale, rcp);
-              qv[8 * c + 2 * e + 1] = quant_fast<BW_DTYPE_F16>(__high2float(h), scale, rcp);
+            for (int t = 0; t < 2; ++t) {
+              const __half2 hh = merged[2 * e + t];
+              v |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(__low2float(hh), scale)))
+                   << (16 * t);
+              v |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(__high2float(hh), scale)))
+                   << (16 * t + 8);
             }
-          }
-          // int8 panel [128 rows x 64 B], 64-byte swizzle: chunk c of row r at c ^ ((r >> 1) & 3)
-          const int swz = (row >> 1) & 3;
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-            *reinterpret_cast<uint4*>(panel + row * 64 + (((2 * half + c) ^ swz) << 4)) =
-                *reinterpret_cast<const uint4*>(&qv[16 * c]);
-          fence_proxy_async_smem();
-          named_bar_sync(1, 256);
-          if (warp == 2 && lane == 0 && k_begin + p * 64 < P.k) {
-            tma_store_2d(&batch.tm_q[pi], panel, k_begin + p * 64, n0);
-            tma_store_commit();
+            qw[e] = v;
           }
         }
-        if (warp == 2 && lane == 0) tma_store_wait0();
+        // this warp's [32 rows x 32 B] int8 block, 32-byte swizzle: chunk c of row r at c ^ ((r >> 2) & 1)
+        uint8_t* buf = stage_q + qbuf * 1024;
+        if (lane == 0) tma_store_wait_read1();  // the store issued from this buffer two panels ago has read it
+        __syncwarp();
+        const int sz = (lane >> 2) & 1;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          *reinterpret_cast<uint4*>(buf + lane * 32 + ((c ^ sz) << 4)) =
+              make_uint4(qw[4 * c], qw[4 * c + 1], qw[4 * c + 2], qw[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int x0 = I.panel * 64 + 32 * half;
+        const int y0 = I.rb * 128 + q * 32;
+        if (lane == 0 && x0 < P.k && y0 < P.n) {
+          tma_store_2d(&batch.tm_q[I.pi], buf, x0, y0);
+          tma_store_commit();
+        }
+        qbuf ^= 1;
       }
     }
+    if (nmine == 0) {
+      // a CTA without items still takes part in the grid barrier
+      __threadfence();
+      named_bar_sync(1, 256);
+      if (warp == 2 && lane == 0) atomicAdd(batch.counter, 1);
+    }
+    if (lane == 0) tma_store_wait0();
   }
 
   tc_fence_before();
-  // All DSMEM traffic of the cluster is finished before any CTA exits; every
-  // wait above is bounded, so every thread of every CTA reaches this point.
-  cluster_sync_all();
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 128);
@@ -684,16 +784,38 @@ static int check_lora_args(const char* op, const void* a, const void* b, int64_t
 static bool req_cluster_eligible(const bw_lora_requant_problem& P) {
   const auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   return lora_tc_ok(P.a, P.b, P.k, P.r) && al16(P.w) && al16(P.q) && (P.ldw * 2) % 16 == 0 && P.ldq % 16 == 0 &&
-         P.k <= 4096 && P.n >= 1 && P.k >= 1;
+         P.n >= 1 && P.k >= 1;
 }
 
-static int launch_req_cluster(const bw_lora_requant_problem* probs, const int* idx, int count, int cluster,
-                              cudaStream_t st) {
+// Items (128-row x 64-column panels) of one problem.
+static int64_t req_items(const bw_lora_requant_problem& P) { return ((P.n + 127) / 128) * ((P.k + 63) / 64); }
+
+static size_t req_workspace_bytes(int64_t items) { return 256 + static_cast<size_t>(items) * 2 * 128 * sizeof(float); }
+
+struct ReqPlan {
+  int smem = 0;
+  int b_bytes = 0, stage_bytes = 0, off_ring = 0, off_q = 0, off_bar = 0;
+};
+
+static ReqPlan req_plan(int rp_max) {
+  ReqPlan pl;
+  const int nbp_max = (rp_max + 63) / 64;
+  pl.b_bytes = nbp_max * 16384;
+  pl.stage_bytes = 16384 + (rp_max * 128 + 1023) / 1024 * 1024;
+  pl.off_ring = 2 * pl.b_bytes;
+  pl.off_q = pl.off_ring + kReqStages * pl.stage_bytes;
+  pl.off_bar = pl.off_q + 8 * 2048;
+  pl.smem = pl.off_bar + 256 + 1024;
+  return pl;
+}
+
+static int launch_req_coop(const bw_lora_requant_problem* probs, const int* idx, int count, void* workspace,
+                           size_t ws_bytes, cudaStream_t st) {
   ReqBatch b;
   memset(&b, 0, sizeof(b));
   b.count = count;
-  b.cluster = cluster;
-  int rp_max = 16, nbp_max = 1, np_max = 1, rb = 0;
+  int rp_max = 16;
+  int64_t items = 0;
   for (int j = 0; j < count; ++j) {
     const bw_lora_requant_problem& P = probs[idx[j]];
     ReqProblem& R = b.p[j];
@@ -704,12 +826,11 @@ static int launch_req_cluster(const bw_lora_requant_problem* probs, const int* i
     R.r = static_cast<int>(P.r);
     R.rp = (R.r + 15) / 16 * 16;
     R.nbp = (R.rp + 63) / 64;
-    R.kc = ((R.k + cluster - 1) / cluster + 63) / 64 * 64;
-    R.rb0 = rb;
-    rb += (R.n + 127) / 128;
+    R.npanel = (R.k + 63) / 64;
+    R.rb = (R.n + 127) / 128;
+    R.item0 = static_cast<int>(items);
+    items += req_items(P);
     rp_max = std::max(rp_max, R.rp);
-    nbp_max = std::max(nbp_max, R.nbp);
-    np_max = std::max(np_max, R.kc / 64);
     if (int e = make_tmap_2d(&b.tm_w[j], P.w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, P.n, P.k, P.ldw * 2, 128, 64,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return e;
@@ -719,61 +840,58 @@ static int launch_req_cluster(const bw_lora_requant_problem* probs, const int* i
     if (int e = make_tmap_2d(&b.tm_b[j], P.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, P.n, P.r, P.r * 2, 128, 64,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return e;
-    if (int e = make_tmap_2d(&b.tm_q[j], P.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, P.n, P.k, P.ldq, 128, 64,
-                             CU_TENSOR_MAP_SWIZZLE_64B))
+    if (int e = make_tmap_2d(&b.tm_q[j], P.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, P.n, P.k, P.ldq, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_32B))
       return e;
   }
-  b.total_rb = rb;
-  b.off_a = nbp_max * 16384;
-  b.off_w = b.off_a + (np_max * rp_max * 128 + 1023) / 1024 * 1024;
-  b.off_red = b.off_w + np_max * 16384;
-  b.off_bar = b.off_red + (256 + kReqMaxCluster * 128) * 4;
-  const int smem = b.off_bar + 128 + 1024;
-  if (smem > 232448) return fail(BW_ERR_UNSUPPORTED, "lora_merge_requant: shared memory plan of %d bytes", smem);
+  if (items > (1LL << 30)) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: problem too large");
+  const size_t need = req_workspace_bytes(items);
+  if (workspace == nullptr || ws_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(BW_ERR_WORKSPACE, "lora_merge_requant: workspace of %zu bytes (256-byte aligned) required, %zu given",
+                need, ws_bytes);
+  b.total_items = static_cast<int>(items);
+  b.counter = static_cast<int*>(workspace);
+  b.maxima = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+  const ReqPlan pl = req_plan(rp_max);
+  b.b_bytes = pl.b_bytes;
+  b.stage_bytes = pl.stage_bytes;
+  b.off_ring = pl.off_ring;
+  b.off_q = pl.off_q;
+  b.off_bar = pl.off_bar;
+  if (pl.smem > 232448) return fail(BW_ERR_UNSUPPORTED, "lora_merge_requant: shared memory plan of %d bytes", pl.smem);
+  int per_sm = 0;
+  if (int e = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_requant_coop_kernel, kReqThreads,
+                                                                      pl.smem),
+                         "cudaOccupancyMaxActiveBlocksPerMultiprocessor(lora_requant_coop_kernel)"))
+    return e;
+  if (per_sm < 1) return fail(BW_ERR_UNSUPPORTED, "lora_merge_requant: kernel does not fit on an SM");
+  const int grid = static_cast<int>(std::min<int64_t>(items, static_cast<int64_t>(per_sm) * num_sms()));
+  if (int e = check_cuda(cudaMemsetAsync(b.counter, 0, sizeof(int), st), "clear requant grid counter")) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(cluster, rb);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kReqThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier cannot deadlock
+  attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, lora_requant_cluster_kernel, b),
-                    "cudaLaunchKernelEx(lora_requant_cluster_kernel)");
+  return check_cuda(cudaLaunchKernelEx(&cfg, lora_requant_coop_kernel, b),
+                    "cudaLaunchKernelEx(lora_requant_coop_kernel)");
 }
 
-// Largest cluster size (16, else 8) the device can co-schedule for this kernel.
-static int req_cluster_size() {
-  static int cached[64] = {0};
-  static std::mutex mu;
+// Kernel attributes, once per device (dynamic shared memory above 48 KB).
+static int req_setup() {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (cached[dev & 63]) return cached[dev & 63];
-  cudaFuncSetAttribute(lora_requant_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 2048);
-  cudaFuncSetAttribute(lora_requant_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  int size = 8;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(16, 1);
-  cfg.blockDim = dim3(kReqThreads);
-  cfg.dynamicSmemBytes = 140 * 1024;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 16;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, lora_requant_cluster_kernel, &cfg) == cudaSuccess && clusters > 0)
-    size = 16;
-  cudaGetLastError();
-  cached[dev & 63] = size;
-  return size;
+  std::call_once(once[dev & 63], [&] {
+    err[dev & 63] = cudaFuncSetAttribute(lora_requant_coop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         232448 - 2048);
+  });
+  return check_cuda(err[dev & 63], "cudaFuncSetAttribute(lora_requant_coop_kernel)");
 }
 
 }  // namespace bw
@@ -867,7 +985,28 @@ static int merge_requant_single(const bw_lora_requant_problem& Pr, cudaStream_t 
 }
 }  // namespace bw
 
-extern "C" int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int count, void* stream) {
+extern "C" size_t bw_lora_merge_requant_batched_workspace_size(const bw_lora_requant_problem* problems, int count) {
+  using namespace bw;
+  // the largest launch: up to kReqMaxProblems eligible problems at a time
+  int64_t best = 0, run = 0;
+  int inrun = 0;
+  for (int i = 0; i < count; ++i) {
+    const bw_lora_requant_problem& P = problems[i];
+    if (P.n <= 0 || P.k <= 0 || !req_cluster_eligible(P)) continue;
+    if (inrun == kReqMaxProblems) {
+      best = std::max(best, run);
+      run = 0;
+      inrun = 0;
+    }
+    run += req_items(P);
+    ++inrun;
+  }
+  best = std::max(best, run);
+  return best > 0 ? req_workspace_bytes(best) : 0;
+}
+
+extern "C" int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int count, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
   using namespace bw;
   if (count < 0 || (count > 0 && problems == nullptr))
     return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: bad problem list");
@@ -883,11 +1022,11 @@ extern "C" int bw_lora_merge_requant_batched(const bw_lora_requant_problem* prob
       return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge_requant: row stride smaller than k (problem %d)", i);
   }
   if (int e = require_sm100()) return e;
-  const int cluster = req_cluster_size();
+  if (int e = req_setup()) return e;
   for (int i = 0; i < count; ++i) {
     const bw_lora_requant_problem& P = problems[i];
     if (P.n == 0) continue;
-    if (req_cluster_eligible(P) && P.k <= static_cast<int64_t>(cluster) * 256) {
+    if (req_cluster_eligible(P)) {
       grouped.push_back(i);
     } else if (int e = merge_requant_single(P, st)) {
       return e;
@@ -895,16 +1034,25 @@ extern "C" int bw_lora_merge_requant_batched(const bw_lora_requant_problem* prob
   }
   for (size_t j = 0; j < grouped.size(); j += kReqMaxProblems) {
     const int c = static_cast<int>(std::min<size_t>(kReqMaxProblems, grouped.size() - j));
-    int64_t kmax = 1;
-    for (int t = 0; t < c; ++t) kmax = std::max(kmax, problems[grouped[j + t]].k);
-    const int csize = static_cast<int>(std::min<int64_t>(cluster, (kmax + 127) / 128));
-    if (int e = launch_req_cluster(problems, grouped.data() + j, c, csize < 1 ? 1 : csize, st)) return e;
+    if (int e = launch_req_coop(problems, grouped.data() + j, c, workspace, workspace_bytes, st)) return e;
   }
   return BW_OK;
 }
 
+extern "C" size_t bw_lora_merge_requant_workspace_size(int64_t n, int64_t k, int64_t r) {
+  bw_lora_requant_problem P = {};
+  P.w = P.a = P.b = reinterpret_cast<const void*>(uintptr_t(256));
+  P.q = reinterpret_cast<int8_t*>(uintptr_t(256));
+  P.ldw = P.ldq = k;
+  P.n = n;
+  P.k = k;
+  P.r = r;
+  return bw_lora_merge_requant_batched_workspace_size(&P, 1);
+}
+
 extern "C" int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, const void* b, float scaling, int8_t* q,
-                                     int64_t ldq, void* scale, int64_t n, int64_t k, int64_t r, void* stream) {
+                                     int64_t ldq, void* scale, int64_t n, int64_t k, int64_t r, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
   bw_lora_requant_problem P;
   P.w = w;
   P.ldw = ldw;
@@ -917,5 +1065,5 @@ extern "C" int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, 
   P.n = n;
   P.k = k;
   P.r = r;
-  return bw_lora_merge_requant_batched(&P, 1, stream);
+  return bw_lora_merge_requant_batched(&P, 1, workspace, workspace_bytes, stream);
 }

@@ -72,4 +72,38 @@ __device__ __forceinline__ int8_t quant_fast(float w, float s, float rcp) {
   return static_cast<int8_t>(fminf(fmaxf(rintf(round_dt<DT>(x)), -127.0f), 127.0f));
 }
 
+// Four fp16 values (two half2 words) -> four int8 codes packed in one word,
+// bit-identical to quant_fast / quant_one with dt = fp16, for a row whose
+// scale is finite and non-zero (so every quotient is finite).  x = RN32(w * rcp)
+// is rounded to fp16 in packed form, clamped to +-127 and rounded to an
+// integer by adding 1536 (fp16 spacing is exactly 1 on [1024, 2048), so the
+// addition is round-to-nearest-even, and the half's low byte is the code).
+// Lanes whose x is within 4 fp32 ulps of an fp16 rounding midpoint redo that
+// element with the exact IEEE division.
+__device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s, float rcp) {
+  const float2 f01 = __half22float2(w01);
+  const float2 f23 = __half22float2(w23);
+  const float x[4] = {__fmul_rn(f01.x, rcp), __fmul_rn(f01.y, rcp), __fmul_rn(f23.x, rcp), __fmul_rn(f23.y, rcp)};
+  const __half2 lim = __float2half2_rn(127.0f);
+  const __half2 nlim = __float2half2_rn(-127.0f);
+  const __half2 bias = __float2half2_rn(1536.0f);
+  __half2 y01 = __hadd2(__hmin2(__hmax2(__floats2half2_rn(x[0], x[1]), nlim), lim), bias);
+  __half2 y23 = __hadd2(__hmin2(__hmax2(__floats2half2_rn(x[2], x[3]), nlim), lim), bias);
+  uint32_t packed;
+  asm("prmt.b32 %0, %1, %2, 0x6420;" : "=r"(packed) : "r"(*reinterpret_cast<uint32_t*>(&y01)),
+      "r"(*reinterpret_cast<uint32_t*>(&y23)));
+  bool near = false;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) near |= ((__float_as_uint(x[e]) + 4u) & 0x1FF8u) == 0x1000u;
+  if (near) {
+    const float f[4] = {f01.x, f01.y, f23.x, f23.y};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t code = static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(f[e], s));
+      packed = (packed & ~(0xFFu << (8 * e))) | (code << (8 * e));
+    }
+  }
+  return packed;
+}
+
 }  // namespace bw

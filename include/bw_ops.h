@@ -121,20 +121,24 @@ int bw_lora_merge(const void* w, int64_t ldw, const void* a, const void* b, floa
 /*
  * Fused delta + merge + per-channel requantisation of the merged weight:
  * (q, scale) = quantize_weight_int8(add_delta(w, lora_delta(a, b, scaling))).
- * The merged fp16 weight is never written to memory and no scratch memory is
- * used.  q [n, k] int8 row stride ldq; scale [n] fp16.
- * Composes lora_ops.cu:16-38 and int8_gemm.py:63-68.
+ * The merged fp16 weight is never written to memory.  q [n, k] int8 row stride
+ * ldq; scale [n] fp16.  Workspace: bw_lora_merge_requant_workspace_size() bytes,
+ * 256-byte aligned, no initialisation needed (per-row panel maxima and a grid
+ * barrier counter that the call clears itself); calls sharing a workspace must
+ * not overlap on the GPU.  Composes lora_ops.cu:16-38 and int8_gemm.py:63-68.
  */
+size_t bw_lora_merge_requant_workspace_size(int64_t n, int64_t k, int64_t r);
 int bw_lora_merge_requant(const void* w, int64_t ldw, const void* a, const void* b, float scaling,
                           int8_t* q, int64_t ldq, void* scale, int64_t n, int64_t k, int64_t r,
-                          void* stream);
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Batched fused merge + requantisation: every problem is
  * (q, scale) = quantize_weight_int8(add_delta(w, lora_delta(a, b, scaling))),
- * e.g. all projections an adapter touches, in as few launches as possible
- * (one per 16 problems with K <= 4096; other shapes run one at a time).
- * Same per-problem contract as bw_lora_merge_requant; no scratch memory.
+ * e.g. all projections an adapter touches, in one launch per 16 problems
+ * (problems TMA cannot address run one at a time).  Same per-problem contract
+ * as bw_lora_merge_requant; one workspace of
+ * bw_lora_merge_requant_batched_workspace_size() bytes serves the whole batch.
  */
 typedef struct bw_lora_requant_problem {
   const void* w;   /* [n, k] fp16, row stride ldw */
@@ -147,7 +151,9 @@ typedef struct bw_lora_requant_problem {
   void* scale;     /* [n] fp16 */
   int64_t n, k, r;
 } bw_lora_requant_problem;
-int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int count, void* stream);
+size_t bw_lora_merge_requant_batched_workspace_size(const bw_lora_requant_problem* problems, int count);
+int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int count, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 
 /*
  * Device-side status of the current device: BW_OK, or BW_ERR_DEVICE_TIMEOUT

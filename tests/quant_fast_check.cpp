@@ -9,7 +9,7 @@
 // arithmetic is IEEE single precision; build without fast-math or FP
 // contraction.
 //
-// usage: quant_fast_check f16|bf16|f32 [scale_stride]
+// usage: quant_fast_check f16|bf16|f32|f16packed [scale_stride]
 //   -> prints "mismatches=<n> slow=<n> total=<n>"; scale_stride > 1 checks every
 //   stride-th scale (all weights) to bound the run time.
 #include <cmath>
@@ -68,6 +68,55 @@ template <int DT> static int8_t quant_fast(float w, float s, float rcp, long* sl
   return static_cast<int8_t>(std::fmin(std::fmax(std::rint(round_dt<DT>(x)), -127.0f), 127.0f));
 }
 
+// Emulation of quant4_f16 (csrc/quant_math.cuh) for one element: packed fp16
+// rounding, fp16 clamp to +-127, +1536 in fp16 (round-to-nearest-even to an
+// integer), code = low byte of the half; exact path when x is near an fp16
+// rounding midpoint.  Valid for finite, non-zero scales.
+static int8_t quant_packed_f16(float w, float s, float rcp, long* slow_count) {
+  volatile float x = w * rcp;
+  if (((f_to_bits(x) + 4u) & 0x1FF8u) == 0x1000u) {
+    ++*slow_count;
+    return quant_exact<F16>(w, s);
+  }
+  _Float16 y = static_cast<_Float16>(x);
+  if (y > static_cast<_Float16>(127.0f)) y = static_cast<_Float16>(127.0f);
+  if (y < static_cast<_Float16>(-127.0f)) y = static_cast<_Float16>(-127.0f);
+  volatile _Float16 z = static_cast<_Float16>(static_cast<float>(y) + 1536.0f);
+  uint16_t bits;
+  _Float16 zz = z;
+  std::memcpy(&bits, &zz, 2);
+  return static_cast<int8_t>(bits & 0xFF);
+}
+
+static void run_packed(int stride) {
+  std::vector<float> scales, weights;
+  for (uint32_t h = 1; h < 0x7C00u; ++h) scales.push_back(f16_to_f(static_cast<uint16_t>(h)));
+  for (uint32_t h = 0; h < 0x10000u; ++h) {
+    const float v = f16_to_f(static_cast<uint16_t>(h));
+    if (std::isfinite(v)) weights.push_back(v);
+  }
+  const int nt = std::max(1u, std::thread::hardware_concurrency());
+  std::vector<long> mism(nt, 0), slow(nt, 0), total(nt, 0);
+  std::vector<std::thread> th;
+  for (int t = 0; t < nt; ++t) {
+    th.emplace_back([&, t] {
+      for (size_t i = static_cast<size_t>(t) * stride; i < scales.size(); i += static_cast<size_t>(nt) * stride) {
+        const float s = scales[i];
+        volatile float one = 1.0f;
+        const float rcp = one / s;
+        for (float w : weights) {
+          if (quant_packed_f16(w, s, rcp, &slow[t]) != quant_exact<F16>(w, s)) ++mism[t];
+          ++total[t];
+        }
+      }
+    });
+  }
+  for (auto& x : th) x.join();
+  long m = 0, sl = 0, tot = 0;
+  for (int t = 0; t < nt; ++t) { m += mism[t]; sl += slow[t]; tot += total[t]; }
+  std::printf("mismatches=%ld slow=%ld total=%ld\n", m, sl, tot);
+}
+
 template <int DT> static void run(int stride) {
   // scales: every non-negative finite value of the dtype (fp32: a dense log sweep)
   std::vector<float> scales, weights;
@@ -117,6 +166,7 @@ int main(int argc, char** argv) {
   if (!std::strcmp(argv[1], "f16")) run<F16>(stride);
   else if (!std::strcmp(argv[1], "bf16")) run<BF16>(stride);
   else if (!std::strcmp(argv[1], "f32")) run<F32>(stride);
+  else if (!std::strcmp(argv[1], "f16packed")) run_packed(stride);
   else return 2;
   return 0;
 }

@@ -3,7 +3,8 @@
 Compiles tests/quant_fast_check.cpp (a C++ restatement of quant_fast /
 quant_one from csrc/quant_math.cuh) and sweeps every finite fp16 / bf16
 weight against every 16th positive scale of the dtype, plus a sampled fp32
-sweep.  The full sweep (every scale: 2.0e9 fp16 and 2.1e9 bf16 pairs) was run
+sweep, and the packed fp16 path (quant4_f16: fp16 clamp and +1536
+round-to-integer) the same way.  The full sweep (every scale: 2.0e9 fp16 and 2.1e9 bf16 pairs) was run
 once with stride 1 and also found no mismatch.
 """
 import shutil
@@ -26,7 +27,7 @@ def checker(tmp_path_factory):
     return exe
 
 
-@pytest.mark.parametrize("dtype,stride", [("f16", 16), ("bf16", 16), ("f32", 1)])
+@pytest.mark.parametrize("dtype,stride", [("f16", 16), ("bf16", 16), ("f32", 1), ("f16packed", 16)])
 def test_fast_quantiser_matches_exact_division(checker, dtype, stride):
     out = subprocess.run([str(checker), dtype, str(stride)], capture_output=True, text=True, check=True).stdout
     fields = dict(kv.split("=") for kv in out.split())
