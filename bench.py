@@ -194,7 +194,7 @@ class MergeRequantWorkload:
             self.problems.append(per_r)
         need = max(self.lib.bw_lora_merge_requant_batched_workspace_size(a, len(QWEN))
                    for per_r in self.problems for a in per_r.values())
-        self.ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        self.ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)  # zero before first use
         self.launches_per_step = len(self.ranks_r)
 
     def config(self):

@@ -29,13 +29,16 @@ _ws: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
-    """Requantisation scratch (panel maxima + grid counter) per (device, stream); no initialisation needed."""
+    """Requantisation scratch (row maxima + counters) per (device, stream).
+
+    Zeroed once at allocation; every call leaves it zero again.
+    """
     if nbytes == 0:
         return None
     key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr(device))
     ws = _ws.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _ws[key] = ws
     return ws
 

@@ -24,11 +24,23 @@ __device__ __forceinline__ float elem_at(const uint8_t* row, int64_t i) {
   else return reinterpret_cast<const float*>(row)[i];
 }
 
+// A NaN scale is stored as the positive quiet NaN that torch produces on the
+// CPU (fp16 0x7E00, bf16 0x7FC0, fp32 0x7FC00000); CUDA's conversions would
+// give 0x7FFF.
+__device__ __forceinline__ __half scale_to_f16(float s) {
+  return s != s ? __ushort_as_half(static_cast<unsigned short>(0x7E00)) : __float2half_rn(s);
+}
+
 template <int DT>
 __device__ __forceinline__ void store_scale(void* scale, int64_t row, float s) {
-  if constexpr (DT == BW_DTYPE_F16) static_cast<__half*>(scale)[row] = __float2half_rn(s);
-  else if constexpr (DT == BW_DTYPE_BF16) static_cast<__nv_bfloat16*>(scale)[row] = __float2bfloat16_rn(s);
-  else static_cast<float*>(scale)[row] = s;
+  if constexpr (DT == BW_DTYPE_F16) {
+    static_cast<__half*>(scale)[row] = scale_to_f16(s);
+  } else if constexpr (DT == BW_DTYPE_BF16) {
+    static_cast<__nv_bfloat16*>(scale)[row] =
+        s != s ? __ushort_as_bfloat16(static_cast<unsigned short>(0x7FC0)) : __float2bfloat16_rn(s);
+  } else {
+    static_cast<float*>(scale)[row] = s != s ? __int_as_float(0x7fc00000) : s;
+  }
 }
 
 // scale from the row's absolute maximum (NaN-propagating like torch.amax)

@@ -41,6 +41,9 @@ EDGE_CASES = [
     ("large_f16", "f16"),
     ("single_nonzero_f16", "f16"),
     ("one_col_f16", "f16"),
+    ("nonfinite_f16", "f16"),
+    ("nonfinite_bf16", "bf16"),
+    ("nonfinite_f32", "f32"),
 ]
 
 # name, seed, M, N, K, x dtype, w dtype
@@ -101,4 +104,13 @@ def edge_weight(name: str, dtype: str) -> np.ndarray:
         return _to_dtype(w, dtype)
     if name.startswith("one_col"):
         return _to_dtype(rng.standard_normal((5, 1), dtype=np.float32), dtype)
+    if name.startswith("nonfinite"):
+        # inf rows (scale inf: finite values -> 0, inf/inf -> NaN -> 0), NaN rows (scale NaN)
+        w = rng.standard_normal((6, 24), dtype=np.float32) * 0.02
+        w[0, 3] = np.inf
+        w[1, 0] = -np.inf
+        w[1, 9] = np.inf
+        w[2, 5] = np.nan
+        w[3, [2, 20]] = [np.nan, np.inf]
+        return _to_dtype(w, dtype)
     raise KeyError(name)

@@ -136,7 +136,7 @@ def test_lora_errors_match_reference_messages(cuda_dev, ops):
 
 
 def test_lora_full_size_70b_requant_properties(cuda_dev, ops):
-    """Llama-3-70B down-projection shard: K = 28672 (224 k-tiles, clusters of 8, two passes)."""
+    """Llama-3-70B down-projection shard: K = 28672 (3584 panels over the resident CTAs, two passes)."""
     cuda, qz = ops
     n, k, r = 1024, 28672, 64
     g = torch.Generator(device=cuda_dev).manual_seed(9)
@@ -169,3 +169,46 @@ def test_lora_merge_requant_batched_equals_single(cuda_dev, ops):
         assert torch.equal(q, q1) and torch.equal(sc, s1)
         qm, sm = quant.quantize_weight_int8(cuda.lora_merge(W, A, B, s).cpu().numpy(), F16)
         assert np.array_equal(q.cpu().numpy(), qm) and np.array_equal(sc.cpu().numpy(), sm)
+
+
+def test_lora_merge_requant_special_rows(cuda_dev, ops):
+    """Rows holding inf, NaN, only zeros or only tiny values take the exact path and match the quantiser."""
+    cuda, qz = ops
+    r, n, k = 16, 256, 512
+    A, B, W = make(700, r, n, k)
+    W = W.copy()
+    W[3, 17] = np.inf
+    W[5, 400] = -np.inf
+    W[7, 1] = np.nan
+    W[9, :] = 0
+    W[11, :] = np.float16(6e-8)   # subnormal row: zero scale after rounding
+    W[130, 300] = np.float16(60000.0)  # near the fp16 maximum: the merge may overflow to inf
+    B[9, :] = 0                   # rows 9 and 11 keep their values through the merge
+    B[11, :] = 0
+    Wd, Ad, Bd = dev16(W, cuda_dev), dev16(A, cuda_dev), dev16(B, cuda_dev)
+    merged = cuda.lora_merge(Wd, Ad, Bd, 2.0)
+    q, sc = cuda.lora_merge_requant(Wd, Ad, Bd, 2.0)
+    q2, sc2 = qz(merged)
+    assert torch.equal(q, q2)
+    assert torch.equal(sc.view(torch.int16), sc2.view(torch.int16))  # NaN scales compare by bits
+    qo, so = quant.quantize_weight_int8(merged.cpu().numpy(), F16)
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(sc.cpu().numpy().view(np.uint16), so.view(np.uint16))
+
+
+def test_lora_merge_requant_many_problems_reuse_workspace(cuda_dev, ops):
+    """More than 16 problems: several launches in a row share one workspace, which each leaves zeroed."""
+    cuda, _ = ops
+    specs = [(16 if i % 2 else 64, 128 * (1 + i % 3), 64 * (2 + i % 5)) for i in range(21)]
+    items = []
+    for i, (r, n, k) in enumerate(specs):
+        A, B, W = make(800 + i, r, n, k)
+        items.append((dev16(W, cuda_dev), dev16(A, cuda_dev), dev16(B, cuda_dev), 1.5))
+    for _ in range(2):
+        outs = cuda.lora_merge_requant_batched(items)
+        for (W, A, B, s), (q, sc) in zip(items, outs):
+            qm, sm = quant.quantize_weight_int8(cuda.lora_merge(W, A, B, s).cpu().numpy(), F16)
+            assert np.array_equal(q.cpu().numpy(), qm) and np.array_equal(sc.cpu().numpy(), sm)
+    torch.cuda.synchronize()
+    for ws in cuda._ws.values():
+        assert int(ws.count_nonzero()) == 0
