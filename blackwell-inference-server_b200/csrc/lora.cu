@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(128)
 //   pass 1: TMA brings the W panel and the A[r, 64] panel into a ring of
 //           stages sized to fill shared memory (and B[128, r] when the row
 //           block changes, double-buffered); tcgen05.mma (M=128, N=64,
-//           K=16 x r/16) -> one of four TMEM accumulator slots; the epilogue
+//           K=16 x r/16) -> one of eight TMEM accumulator slots; the epilogue
 //           merges W' = fp16(W + fp16(acc*s)) in registers (__hadd2 is the
 //           correctly rounded fp16 sum = fp16(fp32(W) + fp32(delta))) and keeps
 //           each row's running |W'| maximum, merged into the workspace's
@@ -209,14 +209,14 @@ __global__ void __launch_bounds__(128)
 //   pass 2: the same panels again (W hits L2, delta recomputed on the tensor
 //           core), row scale from one load of the row maximum, packed exact
 //           quantiser, int8 stored by each warp with its own TMA store.
-// The epilogue is two groups of four warps (thread = row) that take alternate
-// items, so two items are in flight there while the producer and the MMA run
+// The epilogue is four groups of four warps (thread = row) that take the
+// items in turn, so four items are in flight there while the producer and the MMA run
 // up to a full ring ahead (into pass 2 while the epilogue waits at the grid
 // barrier).  The merged weight never touches memory; the workspace holds one
 // word per row and two counters, and the last CTA to leave clears it again.
 // ---------------------------------------------------------------------------
 constexpr int kReqMaxProblems = 16;
-constexpr int kReqGroups = 2;                      // epilogue groups of 4 warps, alternate items
+constexpr int kReqGroups = 4;                      // epilogue groups of 4 warps, items taken in turn
 constexpr int kReqSlots = 2 * kReqGroups;          // TMEM accumulator slots, 64 columns each
 constexpr int kReqThreads = 64 + 128 * kReqGroups; // warp 0 TMA, warp 1 MMA/TMEM, then the epilogue
 constexpr int kReqEpiThreads = 128 * kReqGroups;
@@ -473,63 +473,59 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
           break;
         }
         tc_fence_after();
-        uint32_t acc[64];
-        tmem_ld32(lane_addr + d * 64, *reinterpret_cast<uint32_t(*)[32]>(acc));
-        tmem_ld32(lane_addr + d * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(acc + 32));
         const uint8_t* wrow = sRing + st * batch.stage_bytes + row * 128;
-        uint4 wv[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) wv[c] = *reinterpret_cast<const uint4*>(wrow + ((c ^ sw) << 4));
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&dempty[d]);
-          mbar_arrive(&empty[st]);  // this warp is done with the accumulator slot and the stage
+        const int sz = (lane >> 1) & 3;  // 64-byte swizzle of the int8 staging: chunk c of row r at c ^ ((r >> 1) & 3)
+        if (pass == 1) {
+          if (lane == 0) tma_store_wait_read0();  // the previous store from this warp's buffer has read it
+          __syncwarp();
         }
-        __half2 merged[32];
+        // two 32-column halves: half the registers of a 64-column pass, so four groups fit
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t* w32 = reinterpret_cast<const uint32_t*>(&wv[c]);
+        for (int h = 0; h < 2; ++h) {
+          uint32_t acc[32];
+          tmem_ld32(lane_addr + d * 64 + h * 32, acc);
+          uint4 wv[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __half2 dl = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * P.s,
-                                                 __uint_as_float(acc[8 * c + 2 * e + 1]) * P.s);
-            merged[4 * c + e] = __hadd2(*reinterpret_cast<const __half2*>(&w32[e]), dl);
-          }
-        }
-        if (pass == 0) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) hm = __hmax2_nan(hm, __habs2(merged[e]));
-          continue;
-        }
-        uint32_t qw[16];
-        if (fast_row) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) qw[e] = quant4_f16(merged[2 * e], merged[2 * e + 1], scale, rcp);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            uint32_t v = 0;
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const __half2 hh = merged[2 * e + t];
-              v |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(__low2float(hh), scale)))
-                   << (16 * t);
-              v |= static_cast<uint32_t>(static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(__high2float(hh), scale)))
-                   << (16 * t + 8);
+          for (int c = 0; c < 4; ++c) wv[c] = *reinterpret_cast<const uint4*>(wrow + (((4 * h + c) ^ sw) << 4));
+          tmem_ld_wait();
+          if (h == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(&dempty[d]);
+              mbar_arrive(&empty[st]);  // this warp is done with the accumulator slot and the stage
             }
-            qw[e] = v;
           }
-        }
-        // this warp's [32 rows x 64 B] block; 64-byte swizzle: chunk c of row r at c ^ ((r >> 1) & 3)
-        if (lane == 0) tma_store_wait_read0();  // the previous store from this buffer has read it
-        __syncwarp();
-        const int sz = (lane >> 1) & 3;
+          __half2 merged[16];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sz) << 4)) =
-              make_uint4(qw[4 * c], qw[4 * c + 1], qw[4 * c + 2], qw[4 * c + 3]);
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t* w32 = reinterpret_cast<const uint32_t*>(&wv[c]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __half2 dl = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * P.s,
+                                                   __uint_as_float(acc[8 * c + 2 * e + 1]) * P.s);
+              merged[4 * c + e] = __hadd2(*reinterpret_cast<const __half2*>(&w32[e]), dl);
+            }
+          }
+          if (pass == 0) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) hm = __hmax2_nan(hm, __habs2(merged[e]));
+            continue;
+          }
+          uint32_t qw[8];
+          if (fast_row) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qw[e] = quant4_f16(merged[2 * e], merged[2 * e + 1], scale, rcp);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qw[e] = quant4_special(merged[2 * e], merged[2 * e + 1], scale);
+          }
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            *reinterpret_cast<uint4*>(buf + lane * 64 + (((2 * h + c) ^ sz) << 4)) =
+                make_uint4(qw[4 * c], qw[4 * c + 1], qw[4 * c + 2], qw[4 * c + 3]);
+        }
+        if (pass == 0) continue;
         fence_proxy_async_smem();
         __syncwarp();
         const int x0 = I.panel * 64;

@@ -92,6 +92,24 @@ __device__ __forceinline__ int8_t quant_fast(float w, float s, float rcp) {
 // addition is round-to-nearest-even, and the half's low byte is the code).
 // Lanes whose x is within 4 fp32 ulps of an fp16 rounding midpoint redo that
 // element with the exact IEEE division.
+// Flagged lanes of quant4_f16: redo the elements whose quotient is near a
+// midpoint with the exact division.  Out of line: it runs for a few elements in
+// ten thousand, and inlining it sixteen times per row would crowd the
+// instruction cache of the hot loop.
+static __device__ __noinline__ uint32_t quant4_fix(uint32_t packed, __half2 w01, __half2 w23, float s, float rcp) {
+  const float2 f01 = __half22float2(w01);
+  const float2 f23 = __half22float2(w23);
+  const float f[4] = {f01.x, f01.y, f23.x, f23.y};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (((__float_as_uint(__fmul_rn(f[e], rcp)) + 4u) & 0x1FF8u) == 0x1000u) {
+      const uint32_t code = static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(f[e], s));
+      packed = (packed & ~(0xFFu << (8 * e))) | (code << (8 * e));
+    }
+  }
+  return packed;
+}
+
 __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s, float rcp) {
   const float2 f01 = __half22float2(w01);
   const float2 f23 = __half22float2(w23);
@@ -107,14 +125,23 @@ __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s
   bool near = false;
 #pragma unroll
   for (int e = 0; e < 4; ++e) near |= ((__float_as_uint(x[e]) + 4u) & 0x1FF8u) == 0x1000u;
-  if (near) {
-    const float f[4] = {f01.x, f01.y, f23.x, f23.y};
+  if (near) packed = quant4_fix(packed, w01, w23, s, rcp);
+  return packed;
+}
+
+// quant_one<fp16>'s codes, four at a time, for a row whose scale is not a
+// finite positive number, in closed form: a NaN or +inf scale gives 0 for
+// every element (w / inf = 0, inf / inf = NaN -> 0); a zero scale (a row of
+// zeros and values below fp16's subnormal step) gives +-127 by sign and 0 for
+// +-0 (0 / 0 = NaN -> 0).  Such a row holds no NaN or inf when its scale is 0.
+__device__ __forceinline__ uint32_t quant4_special(__half2 w01, __half2 w23, float s) {
+  if (s != 0.0f) return 0u;
+  const float2 f01 = __half22float2(w01);
+  const float2 f23 = __half22float2(w23);
+  const float f[4] = {f01.x, f01.y, f23.x, f23.y};
+  uint32_t packed = 0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const uint32_t code = static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(f[e], s));
-      packed = (packed & ~(0xFFu << (8 * e))) | (code << (8 * e));
-    }
-  }
+  for (int e = 0; e < 4; ++e) packed |= (f[e] > 0.0f ? 0x7Fu : (f[e] < 0.0f ? 0x81u : 0u)) << (8 * e);
   return packed;
 }
 
