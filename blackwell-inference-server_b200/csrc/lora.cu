@@ -222,6 +222,7 @@ constexpr int kReqThreads = 64 + 128 * kReqGroups; // warp 0 TMA, warp 1 MMA/TME
 constexpr int kReqEpiThreads = 128 * kReqGroups;
 constexpr int kReqMaxStages = 12;
 constexpr int kReqSmemLimit = 232448;              // 227 KB of dynamic shared memory per CTA
+constexpr int kReqBarBytes = 1536;                 // mbarriers and flags (512 B), then the problem table
 
 struct ReqProblem {
   __half* scale;
@@ -258,19 +259,35 @@ enum ReqWaitSite : int {
   kSiteReqBEmpty = 218,
 };
 
-struct ReqItem {
+// Position of an item in the batch: problem, row block, panel.  The roles walk
+// their items with these, reading the problem table from shared memory (the
+// kernel-parameter copy is reached through generic loads that every asm
+// "memory" clobber would force to be re-issued).
+struct ReqWalk {
   int pi, rb, panel;
 };
 
-__device__ __forceinline__ ReqItem req_item(const ReqBatch& bt, int item) {
+__device__ __forceinline__ ReqWalk req_walk_at(const ReqProblem* sp, int count, int item) {
   int pi = 0;
-  while (pi + 1 < bt.count && bt.p[pi + 1].item0 <= item) ++pi;
-  const int local = item - bt.p[pi].item0;
-  ReqItem r;
-  r.pi = pi;
-  r.rb = local / bt.p[pi].npanel;
-  r.panel = local % bt.p[pi].npanel;
-  return r;
+  while (pi + 1 < count && sp[pi + 1].item0 <= item) ++pi;
+  const int local = item - sp[pi].item0;
+  const int np = sp[pi].npanel;
+  ReqWalk w;
+  w.pi = pi;
+  w.rb = local / np;
+  w.panel = local - w.rb * np;
+  return w;
+}
+
+__device__ __forceinline__ void req_walk_next(ReqWalk& w, const ReqProblem* sp, int count) {
+  if (w.pi >= count) return;
+  if (++w.panel == sp[w.pi].npanel) {
+    w.panel = 0;
+    if (++w.rb == sp[w.pi].rb) {
+      w.rb = 0;
+      ++w.pi;
+    }
+  }
 }
 
 // |W'| maximum of a half2 running max as float bits, NaN if either half is NaN.
@@ -279,10 +296,20 @@ __device__ __forceinline__ unsigned req_max_bits(__half2 hm) {
   return (l != l || h != h) ? 0x7fc00000u : __float_as_uint(fmaxf(l, h));
 }
 
+static_assert(512 + kReqMaxProblems * sizeof(ReqProblem) <= kReqBarBytes, "problem table does not fit");
+
 __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const __grid_constant__ ReqBatch batch) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // kernel-wide values in registers
   const int S = batch.stages;
+  const int count = batch.count;
+  const int b_bytes = batch.b_bytes;
+  const int stage_bytes = batch.stage_bytes;
+  const int T = batch.total_items;
+  int* const gsync = batch.sync;
+  unsigned* const rowmax = batch.rowmax;
+  const int total_rows = batch.total_rows;
   uint8_t* sB = smem;                                  // 2 x b_bytes
   uint8_t* sRing = smem + batch.off_ring;              // S x stage_bytes
   uint8_t* sQ = smem + batch.off_q;                    // one 2 KB int8 staging buffer per epilogue warp
@@ -296,11 +323,11 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_cta = abort_flag + 1;
+  ReqProblem* sp = reinterpret_cast<ReqProblem*>(smem + batch.off_bar + 512);  // problem table
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int G = static_cast<int>(gridDim.x);
-  const int T = batch.total_items;
   const int lo = static_cast<int>((static_cast<long long>(T) * blockIdx.x) / G);
   const int hi = static_cast<int>((static_cast<long long>(T) * (blockIdx.x + 1)) / G);
   const int nmine = hi - lo;    // >= 1: the host launches at most one CTA per item
@@ -324,6 +351,13 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
     *last_cta = 0;
     fence_mbar_init();
   }
+  if (warp == 0 && lane < count) {
+    tma_prefetch_desc(&batch.tm_w[lane]);
+    tma_prefetch_desc(&batch.tm_a[lane]);
+    tma_prefetch_desc(&batch.tm_b[lane]);
+    tma_prefetch_desc(&batch.tm_q[lane]);
+  }
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + count) sp[threadIdx.x - 64] = batch.p[threadIdx.x - 64];
   if (warp == 1) {
     tmem_alloc(tmem_slot, kReqSlots * 64);
     tmem_relinquish();
@@ -340,44 +374,57 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
     if (lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
       const uint64_t once = l2_policy_evict_first();
-      int prev_key = -1, bseq = -1;
+      int bseq = -1;
+      ReqWalk w = req_walk_at(sp, count, lo);
+      int prev_pi = -1, prev_rb = -1;
       for (int it = 0; it < steps; ++it) {
-        const int item = lo + (it % nmine);
-        const ReqItem I = req_item(batch, item);
-        const ReqProblem& P = batch.p[I.pi];
-        const int key = item - I.panel;  // first item of the row block: identifies (problem, row block)
-        if (key != prev_key || it == nmine) {
-          prev_key = key;
+        if (it == nmine) {
+          w = req_walk_at(sp, count, lo);
+          prev_pi = -1;  // pass 2 starts with a fresh B buffer
+        }
+        const int pi = w.pi, rb = w.rb, panel = w.panel;
+        const int nbp = sp[pi].nbp;
+        const int a_bytes = sp[pi].rp * 128;
+        if (pi != prev_pi || rb != prev_rb) {
+          prev_pi = pi;
+          prev_rb = rb;
           ++bseq;
           const int bb = bseq & 1;
           // the buffer's previous row block must be finished by the MMA
           if (!mbar_wait(&bempty[bb], ((bseq >> 1) & 1) ^ 1, abort_flag, kSiteReqBEmpty)) break;
-          mbar_arrive_expect_tx(&bfull[bb], P.nbp * 16384);
-          for (int p = 0; p < P.nbp; ++p)
-            tma_load_2d(sB + bb * batch.b_bytes + p * 16384, &batch.tm_b[I.pi], &bfull[bb], p * 64, I.rb * 128, keep);
+          mbar_arrive_expect_tx(&bfull[bb], nbp * 16384);
+          for (int p = 0; p < nbp; ++p)
+            tma_load_2d(sB + bb * b_bytes + p * 16384, &batch.tm_b[pi], &bfull[bb], p * 64, rb * 128, keep);
         }
         const int st = it % S;
         if (!mbar_wait(&empty[st], ((it / S) & 1) ^ 1, abort_flag, kSiteReqEmpty)) break;
-        uint8_t* slot = sRing + st * batch.stage_bytes;
-        mbar_arrive_expect_tx(&full[st], 16384 + P.rp * 128);
-        const int kx = I.panel * 64;
-        tma_load_2d(slot, &batch.tm_w[I.pi], &full[st], kx, I.rb * 128, it < nmine ? keep : once);
-        tma_load_2d(slot + 16384, &batch.tm_a[I.pi], &full[st], kx, 0, keep);
+        uint8_t* slot = sRing + st * stage_bytes;
+        mbar_arrive_expect_tx(&full[st], 16384 + a_bytes);
+        tma_load_2d(slot, &batch.tm_w[pi], &full[st], panel * 64, rb * 128, it < nmine ? keep : once);
+        tma_load_2d(slot + 16384, &batch.tm_a[pi], &full[st], panel * 64, 0, keep);
+        req_walk_next(w, sp, count);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(128, 64, false, true);
-      int prev_key = -1, bseq = -1;
+      const uint32_t sB_u32 = smem_u32(sB);
+      const uint32_t ring_u32 = smem_u32(sRing) + 16384;  // A panel of stage 0
+      int bseq = -1;
+      ReqWalk w = req_walk_at(sp, count, lo);
+      int prev_pi = -1, prev_rb = -1;
       for (int it = 0; it < steps; ++it) {
-        const int item = lo + (it % nmine);
-        const ReqItem I = req_item(batch, item);
-        const ReqProblem& P = batch.p[I.pi];
-        const int key = item - I.panel;
-        if (key != prev_key || it == nmine) {
+        if (it == nmine) {
+          w = req_walk_at(sp, count, lo);
+          prev_pi = -1;
+        }
+        const int pi = w.pi, rb = w.rb;
+        const int rp = sp[pi].rp;
+        if (pi != prev_pi || rb != prev_rb) {
           if (bseq >= 0) umma_commit(&bempty[bseq & 1]);  // previous row block's MMAs release its B buffer
-          prev_key = key;
+          prev_pi = pi;
+          prev_rb = rb;
           ++bseq;
           if (!mbar_wait(&bfull[bseq & 1], (bseq >> 1) & 1, abort_flag, kSiteReqB)) break;
         }
@@ -387,15 +434,16 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             !mbar_wait(&dempty[d], ((it / kReqSlots) & 1) ^ 1, abort_flag, kSiteReqDE))
           break;
         tc_fence_after();
-        const uint32_t b_base = smem_u32(sB + (bseq & 1) * batch.b_bytes);
-        const uint32_t a_base = smem_u32(sRing + st * batch.stage_bytes + 16384);
-        for (int kk = 0; kk < P.rp / 16; ++kk) {
+        const uint32_t b_base = sB_u32 + (bseq & 1) * b_bytes;
+        const uint32_t a_base = ring_u32 + st * stage_bytes;
+        for (int kk = 0; kk < rp / 16; ++kk) {
           const uint64_t ad = make_sdesc(b_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-          const uint64_t bd = make_sdesc(a_base + kk * 2048, P.rp * 128, 1024, kLayoutSW128);
+          const uint64_t bd = make_sdesc(a_base + kk * 2048, rp * 128, 1024, kLayoutSW128);
           umma_f16(tmem + d * 64, ad, bd, idesc, kk > 0 ? 1u : 0u);
         }
         umma_commit(&dfull[d]);
         umma_commit(&empty[st]);
+        req_walk_next(w, sp, count);
       }
       umma_commit(final_bar);  // every issued MMA has completed before TMEM is freed
       mbar_wait(final_bar, 0, nullptr, kSiteReqFinal);
@@ -409,6 +457,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
     const int sw = row & 7;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint8_t* buf = sQ + ew * 2048;       // [32 rows x 64 B] int8, 64-byte swizzle
+    const int sz = (lane >> 1) & 3;      // chunk c of staging row r sits at c ^ ((r >> 1) & 3)
     bool bad = false;
     for (int pass = 0; pass < 2; ++pass) {
       if (pass == 1) {
@@ -418,10 +467,10 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         // only the spinning thread knows the outcome: it alone votes, the OR spreads it
         bool grid_failed = false;
         if (ew == 0 && lane == 0) {
-          atomicAdd(&batch.sync[0], 1);
+          atomicAdd(&gsync[0], 1);
           const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
           const long long t0 = clock64();
-          while (atomicAdd(&batch.sync[0], 0) < G) {
+          while (atomicAdd(&gsync[0], 0) < G) {
             if (clock64() - t0 > limit) {
               record_timeout(kSiteReqGrid);
               grid_failed = true;
@@ -434,36 +483,40 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         if (named_bar_any(1, kReqEpiThreads, grid_failed)) bad = true;
         __threadfence();
       }
-      int cur_key = -1, cur_row = -1;
+      int cur_pi = -1, cur_rb = -1, cur_row = -1;
       __half2 hm = __float2half2_rn(0.0f);
-      float scale = 0.f, rcp = 0.f;
+      float scale = 0.f, rcp = 0.f, s = 0.f;
       bool fast_row = false;
+      int pn = 0;
       const int it0 = pass * nmine;
-      for (int it = it0 + ((grp - it0 % kReqGroups) + kReqGroups) % kReqGroups; it < it0 + nmine;
-           it += kReqGroups) {
+      const int first = it0 + ((grp - it0 % kReqGroups) + kReqGroups) % kReqGroups;
+      ReqWalk w = req_walk_at(sp, count, lo + (first - it0));
+      for (int it = first; it < it0 + nmine; it += kReqGroups) {
         if (bad) break;
-        const int item = lo + (it % nmine);
-        const ReqItem I = req_item(batch, item);
-        const ReqProblem& P = batch.p[I.pi];
         const int st = it % S;
         const int d = it % kReqSlots;
-        const int key = item - I.panel;
-        const int n = I.rb * 128 + row;
-        if (key != cur_key) {
+        const int n = w.rb * 128 + row;
+        if (w.pi != cur_pi || w.rb != cur_rb) {
+          if (w.pi != cur_pi) {
+            s = sp[w.pi].s;
+            pn = sp[w.pi].n;
+          }
+          const int grow = sp[w.pi].row0 + n;
           if (pass == 0) {
             // fold the finished row block's maximum into the workspace
-            if (cur_row >= 0) atomicMax(&batch.rowmax[cur_row], req_max_bits(hm));
+            if (cur_row >= 0) atomicMax(&rowmax[cur_row], req_max_bits(hm));
             hm = __float2half2_rn(0.0f);
-          } else if (n < P.n) {
-            const float m = __uint_as_float(__ldcg(&batch.rowmax[P.row0 + n]));
+          } else if (n < pn) {
+            const float m = __uint_as_float(__ldcg(&rowmax[grow]));
             scale = scale_from_amax<BW_DTYPE_F16>(m, m != m);
             rcp = __frcp_rn(scale);
             // finite, non-zero scale: every quotient is finite and the packed path applies
             fast_row = scale > 0.0f && scale < __int_as_float(0x7f800000) && rcp < 1.0e30f;
-            if (I.panel == 0) P.scale[n] = scale_to_f16(scale);
+            if (w.panel == 0) sp[w.pi].scale[n] = scale_to_f16(scale);
           }
-          cur_key = key;
-          cur_row = n < P.n ? P.row0 + n : -1;
+          cur_pi = w.pi;
+          cur_rb = w.rb;
+          cur_row = n < pn ? grow : -1;
         }
         bool ok = mbar_wait(&dfull[d], (it / kReqSlots) & 1, abort_flag, kSiteReqD) &&
                   mbar_wait(&full[st], (it / S) & 1, abort_flag, kSiteReqFull);
@@ -473,8 +526,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
           break;
         }
         tc_fence_after();
-        const uint8_t* wrow = sRing + st * batch.stage_bytes + row * 128;
-        const int sz = (lane >> 1) & 3;  // 64-byte swizzle of the int8 staging: chunk c of row r at c ^ ((r >> 1) & 3)
+        const uint8_t* wrow = sRing + st * stage_bytes + row * 128;
         if (pass == 1) {
           if (lane == 0) tma_store_wait_read0();  // the previous store from this warp's buffer has read it
           __syncwarp();
@@ -502,8 +554,8 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             const uint32_t* w32 = reinterpret_cast<const uint32_t*>(&wv[c]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const __half2 dl = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * P.s,
-                                                   __uint_as_float(acc[8 * c + 2 * e + 1]) * P.s);
+              const __half2 dl = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * s,
+                                                   __uint_as_float(acc[8 * c + 2 * e + 1]) * s);
               merged[4 * c + e] = __hadd2(*reinterpret_cast<const __half2*>(&w32[e]), dl);
             }
           }
@@ -525,30 +577,32 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             *reinterpret_cast<uint4*>(buf + lane * 64 + (((2 * h + c) ^ sz) << 4)) =
                 make_uint4(qw[4 * c], qw[4 * c + 1], qw[4 * c + 2], qw[4 * c + 3]);
         }
-        if (pass == 0) continue;
-        fence_proxy_async_smem();
-        __syncwarp();
-        const int x0 = I.panel * 64;
-        const int y0 = I.rb * 128 + q * 32;
-        if (lane == 0 && y0 < P.n) {
-          tma_store_2d(&batch.tm_q[I.pi], buf, x0, y0);
-          tma_store_commit();
+        if (pass == 1) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          const int y0 = w.rb * 128 + q * 32;
+          if (lane == 0 && y0 < pn) {
+            tma_store_2d(&batch.tm_q[w.pi], buf, w.panel * 64, y0);
+            tma_store_commit();
+          }
         }
+#pragma unroll
+        for (int j = 0; j < kReqGroups; ++j) req_walk_next(w, sp, count);
       }
-      if (pass == 0 && !bad && cur_row >= 0) atomicMax(&batch.rowmax[cur_row], req_max_bits(hm));
+      if (pass == 0 && !bad && cur_row >= 0) atomicMax(&rowmax[cur_row], req_max_bits(hm));
     }
     if (lane == 0) tma_store_wait0();
     // ---- exit: the last CTA out clears the workspace for the next call ----
     __threadfence();
     named_bar_sync(1, kReqEpiThreads);
-    if (ew == 0 && lane == 0) *last_cta = atomicAdd(&batch.sync[1], 1) == G - 1 ? 1 : 0;
+    if (ew == 0 && lane == 0) *last_cta = atomicAdd(&gsync[1], 1) == G - 1 ? 1 : 0;
     named_bar_sync(1, kReqEpiThreads);
     if (*last_cta) {
       __threadfence();
-      for (int i = threadIdx.x - 64; i < batch.total_rows; i += kReqEpiThreads) __stcg(&batch.rowmax[i], 0u);
+      for (int i = threadIdx.x - 64; i < total_rows; i += kReqEpiThreads) __stcg(&rowmax[i], 0u);
       if (ew == 0 && lane == 0) {
-        atomicExch(&batch.sync[0], 0);
-        atomicExch(&batch.sync[1], 0);
+        atomicExch(&gsync[0], 0);
+        atomicExch(&gsync[1], 0);
       }
     }
   }
@@ -706,7 +760,7 @@ struct ReqPlan {
   int b_bytes = 0, stage_bytes = 0, off_ring = 0, off_q = 0, off_bar = 0;
 };
 
-// Shared memory: 2 B buffers, as many ring stages as fit, int8 staging, barriers.
+// Shared memory: 2 B buffers, as many ring stages as fit, int8 staging, barriers + problem table.
 static ReqPlan req_plan(int rp_max) {
   ReqPlan pl;
   const int nbp_max = (rp_max + 63) / 64;
@@ -714,11 +768,11 @@ static ReqPlan req_plan(int rp_max) {
   pl.stage_bytes = 16384 + (rp_max * 128 + 1023) / 1024 * 1024;
   pl.off_ring = 2 * pl.b_bytes;
   const int staging = 4 * kReqGroups * 2048;
-  const int fixed = pl.off_ring + staging + 512 + 1024;
+  const int fixed = pl.off_ring + staging + kReqBarBytes + 1024;
   pl.stages = std::min(kReqMaxStages, (kReqSmemLimit - fixed) / pl.stage_bytes);
   pl.off_q = pl.off_ring + pl.stages * pl.stage_bytes;
   pl.off_bar = pl.off_q + staging;
-  pl.smem = pl.off_bar + 512 + 1024;
+  pl.smem = pl.off_bar + kReqBarBytes + 1024;
   return pl;
 }
 
