@@ -218,6 +218,8 @@ __global__ void __launch_bounds__(128)
 constexpr int kReqMaxProblems = 16;
 constexpr int kReqGroups = 4;                      // epilogue groups of 4 warps, items taken in turn
 constexpr int kReqSlots = 2 * kReqGroups;          // TMEM accumulator slots, 64 columns each
+constexpr int kReqTmemCols = kReqSlots * 64 <= 256 ? 256 : 512;  // allocation: a power of two
+static_assert(kReqSlots * 64 <= 512, "TMEM holds 512 columns");
 constexpr int kReqThreads = 64 + 128 * kReqGroups; // warp 0 TMA, warp 1 MMA/TMEM, then the epilogue
 constexpr int kReqEpiThreads = 128 * kReqGroups;
 constexpr int kReqMaxStages = 12;
@@ -359,7 +361,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + count) sp[threadIdx.x - 64] = batch.p[threadIdx.x - 64];
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kReqSlots * 64);
+    tmem_alloc(tmem_slot, kReqTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -486,7 +488,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
       int cur_pi = -1, cur_rb = -1, cur_row = -1;
       __half2 hm = __float2half2_rn(0.0f);
       float scale = 0.f, rcp = 0.f, s = 0.f;
-      bool fast_row = false;
+      bool fast_row = false, normal_row = false;
       int pn = 0;
       const int it0 = pass * nmine;
       const int first = it0 + ((grp - it0 % kReqGroups) + kReqGroups) % kReqGroups;
@@ -512,6 +514,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             rcp = __frcp_rn(scale);
             // finite, non-zero scale: every quotient is finite and the packed path applies
             fast_row = scale > 0.0f && scale < __int_as_float(0x7f800000) && rcp < 1.0e30f;
+            normal_row = fast_row && scale >= 6.103515625e-05f;  // no clamp needed (quant4_f16<false>)
             if (w.panel == 0) sp[w.pi].scale[n] = scale_to_f16(scale);
           }
           cur_pi = w.pi;
@@ -565,9 +568,12 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             continue;
           }
           uint32_t qw[8];
-          if (fast_row) {
+          if (normal_row) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) qw[e] = quant4_f16(merged[2 * e], merged[2 * e + 1], scale, rcp);
+            for (int e = 0; e < 8; ++e) qw[e] = quant4_f16<false>(merged[2 * e], merged[2 * e + 1], scale, rcp);
+          } else if (fast_row) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qw[e] = quant4_f16<true>(merged[2 * e], merged[2 * e + 1], scale, rcp);
           } else {
 #pragma unroll
             for (int e = 0; e < 8; ++e) qw[e] = quant4_special(merged[2 * e], merged[2 * e + 1], scale);
@@ -611,7 +617,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kReqSlots * 64);
+    tmem_dealloc(tmem, kReqTmemCols);
   }
 }
 

@@ -110,15 +110,25 @@ static __device__ __noinline__ uint32_t quant4_fix(uint32_t packed, __half2 w01,
   return packed;
 }
 
+// CLAMP = false is for rows whose scale is a normal fp16 number (>= 2^-14):
+// then every |w| <= the row maximum gives |x| < 127.07, fp16(x) stays within
+// +-127.0625 and the rounding lands on codes -127..127 without the clamp.
+template <bool CLAMP = true>
 __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s, float rcp) {
   const float2 f01 = __half22float2(w01);
   const float2 f23 = __half22float2(w23);
   const float x[4] = {__fmul_rn(f01.x, rcp), __fmul_rn(f01.y, rcp), __fmul_rn(f23.x, rcp), __fmul_rn(f23.y, rcp)};
-  const __half2 lim = __float2half2_rn(127.0f);
-  const __half2 nlim = __float2half2_rn(-127.0f);
   const __half2 bias = __float2half2_rn(1536.0f);
-  __half2 y01 = __hadd2(__hmin2(__hmax2(__floats2half2_rn(x[0], x[1]), nlim), lim), bias);
-  __half2 y23 = __hadd2(__hmin2(__hmax2(__floats2half2_rn(x[2], x[3]), nlim), lim), bias);
+  __half2 y01 = __floats2half2_rn(x[0], x[1]);
+  __half2 y23 = __floats2half2_rn(x[2], x[3]);
+  if constexpr (CLAMP) {
+    const __half2 lim = __float2half2_rn(127.0f);
+    const __half2 nlim = __float2half2_rn(-127.0f);
+    y01 = __hmin2(__hmax2(y01, nlim), lim);
+    y23 = __hmin2(__hmax2(y23, nlim), lim);
+  }
+  y01 = __hadd2(y01, bias);
+  y23 = __hadd2(y23, bias);
   uint32_t packed;
   asm("prmt.b32 %0, %1, %2, 0x6420;" : "=r"(packed) : "r"(*reinterpret_cast<uint32_t*>(&y01)),
       "r"(*reinterpret_cast<uint32_t*>(&y23)));

@@ -9,7 +9,7 @@
 // arithmetic is IEEE single precision; build without fast-math or FP
 // contraction.
 //
-// usage: quant_fast_check f16|bf16|f32|f16packed [scale_stride]
+// usage: quant_fast_check f16|bf16|f32|f16packed|f16packed_noclamp [scale_stride]
 //   -> prints "mismatches=<n> slow=<n> total=<n>"; scale_stride > 1 checks every
 //   stride-th scale (all weights) to bound the run time.
 #include <cmath>
@@ -86,6 +86,64 @@ static int8_t quant_packed_f16(float w, float s, float rcp, long* slow_count) {
   _Float16 zz = z;
   std::memcpy(&bits, &zz, 2);
   return static_cast<int8_t>(bits & 0xFF);
+}
+
+// quant4_f16 without the +-127 clamp, used for rows whose scale is a normal
+// fp16 number: every |w| <= amax of the row gives |x| < 127.07, so fp16(x)
+// stays within +-127.0625 and the +1536 rounding lands on 1409..1663.
+static int8_t quant_packed_f16_noclamp(float w, float s, float rcp, long* slow_count) {
+  volatile float x = w * rcp;
+  if (((f_to_bits(x) + 4u) & 0x1FF8u) == 0x1000u) {
+    ++*slow_count;
+    return quant_exact<F16>(w, s);
+  }
+  const _Float16 y = static_cast<_Float16>(x);
+  volatile _Float16 z = static_cast<_Float16>(static_cast<float>(y) + 1536.0f);
+  uint16_t bits;
+  _Float16 zz = z;
+  std::memcpy(&bits, &zz, 2);
+  return static_cast<int8_t>(bits & 0xFF);
+}
+
+// Every (w, s) a row can hold: s = the quantiser's scale of the row maximum a
+// (csrc/quant_math.cuh: scale_from_amax), |w| <= a, s normal (>= 2^-14).
+static void run_packed_noclamp(int stride) {
+  std::vector<float> scale_of, amax_of;  // distinct scales with the largest row maximum giving each
+  for (uint32_t h = 1; h < 0x7C00u; ++h) {
+    const float a = f16_to_f(static_cast<uint16_t>(h));
+    volatile float den = 127.0f;
+    const float amaxc = round_f16(std::fmax(a, 1e-8f));
+    const float s = round_f16(amaxc / den);
+    if (!(s >= 6.103515625e-05f) || !std::isfinite(s)) continue;
+    if (!scale_of.empty() && scale_of.back() == s) amax_of.back() = a;
+    else { scale_of.push_back(s); amax_of.push_back(a); }
+  }
+  std::vector<float> weights;
+  for (uint32_t h = 0; h < 0x10000u; ++h) {
+    const float v = f16_to_f(static_cast<uint16_t>(h));
+    if (std::isfinite(v)) weights.push_back(v);
+  }
+  const int nt = std::max(1u, std::thread::hardware_concurrency());
+  std::vector<long> mism(nt, 0), slow(nt, 0), total(nt, 0);
+  std::vector<std::thread> th;
+  for (int t = 0; t < nt; ++t) {
+    th.emplace_back([&, t] {
+      for (size_t i = static_cast<size_t>(t) * stride; i < scale_of.size(); i += static_cast<size_t>(nt) * stride) {
+        const float s = scale_of[i], a = amax_of[i];
+        volatile float one = 1.0f;
+        const float rcp = one / s;
+        for (float w : weights) {
+          if (std::fabs(w) > a) continue;
+          if (quant_packed_f16_noclamp(w, s, rcp, &slow[t]) != quant_exact<F16>(w, s)) ++mism[t];
+          ++total[t];
+        }
+      }
+    });
+  }
+  for (auto& x : th) x.join();
+  long m = 0, sl = 0, tot = 0;
+  for (int t = 0; t < nt; ++t) { m += mism[t]; sl += slow[t]; tot += total[t]; }
+  std::printf("mismatches=%ld slow=%ld total=%ld\n", m, sl, tot);
 }
 
 static void run_packed(int stride) {
@@ -167,6 +225,7 @@ int main(int argc, char** argv) {
   else if (!std::strcmp(argv[1], "bf16")) run<BF16>(stride);
   else if (!std::strcmp(argv[1], "f32")) run<F32>(stride);
   else if (!std::strcmp(argv[1], "f16packed")) run_packed(stride);
+  else if (!std::strcmp(argv[1], "f16packed_noclamp")) run_packed_noclamp(stride);
   else return 2;
   return 0;
 }

@@ -183,8 +183,10 @@ def test_lora_merge_requant_special_rows(cuda_dev, ops):
     W[9, :] = 0
     W[11, :] = np.float16(6e-8)   # subnormal row: zero scale after rounding
     W[130, 300] = np.float16(60000.0)  # near the fp16 maximum: the merge may overflow to inf
-    B[9, :] = 0                   # rows 9 and 11 keep their values through the merge
+    W[13, :] = (np.linspace(-1, 1, k) * 3e-4).astype(np.float16)  # subnormal scale: the clamped packed path
+    B[9, :] = 0                   # rows 9, 11 and 13 keep their values through the merge
     B[11, :] = 0
+    B[13, :] = 0
     Wd, Ad, Bd = dev16(W, cuda_dev), dev16(A, cuda_dev), dev16(B, cuda_dev)
     merged = cuda.lora_merge(Wd, Ad, Bd, 2.0)
     q, sc = cuda.lora_merge_requant(Wd, Ad, Bd, 2.0)
