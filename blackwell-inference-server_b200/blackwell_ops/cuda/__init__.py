@@ -29,9 +29,11 @@ _ws: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
-    """Requantisation scratch (row maxima + counters) per (device, stream).
+    """Requantisation scratch (grid barrier + two sets of row maxima) per (device, stream).
 
-    Zeroed once at allocation; every call leaves it zero again.
+    Zeroed once at allocation and always passed with its full size: each call
+    clears the set of row maxima the next call uses.  A larger need replaces it
+    with a new zeroed buffer.
     """
     if nbytes == 0:
         return None
@@ -149,7 +151,8 @@ def lora_merge_requant(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
     with torch.cuda.device(W.device):
         check(lib.bw_lora_merge_requant(W.data_ptr(), W.stride(0), A.data_ptr(), B.data_ptr(), float(scaling),
                                         q.data_ptr(), K, scale.data_ptr(), N, K, r,
-                                        ws.data_ptr() if ws is not None else None, nbytes, stream_ptr(W.device)),
+                                        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                                        stream_ptr(W.device)),
               "lora_merge_requant")
     return q, scale
 
@@ -197,7 +200,8 @@ def lora_merge_requant_batched(items):
         ws = _workspace(dev, nbytes)
         with torch.cuda.device(dev):
             check(lib.bw_lora_merge_requant_batched(arr, len(probs), ws.data_ptr() if ws is not None else None,
-                                                    nbytes, stream_ptr(dev)), "lora_merge_requant_batched")
+                                                    ws.numel() if ws is not None else 0, stream_ptr(dev)),
+                  "lora_merge_requant_batched")
     return outs
 
 

@@ -29,6 +29,13 @@ extern __device__ int g_status;  // 0 = ok, else wait-site id
 
 __device__ __forceinline__ void record_timeout(int site) { atomicCAS(&g_status, 0, site); }
 
+// Acquire load at GPU scope (a flag another CTA publishes with a release or a fence).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

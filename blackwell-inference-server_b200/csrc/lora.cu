@@ -205,15 +205,18 @@ __global__ void __launch_bounds__(128)
 //           correctly rounded fp16 sum = fp16(fp32(W) + fp32(delta))) and keeps
 //           each row's running |W'| maximum, merged into the workspace's
 //           per-row maxima with one atomicMax per row block;
-//   grid barrier (bounded spin on a workspace counter; every CTA is resident);
+//   grid barrier (a self-resetting generation barrier in the workspace; every
+//           CTA is resident, the wait is bounded);
 //   pass 2: the same panels again (W hits L2, delta recomputed on the tensor
 //           core), row scale from one load of the row maximum, packed exact
 //           quantiser, int8 stored by each warp with its own TMA store.
 // The epilogue is four groups of four warps (thread = row) that take the
-// items in turn, so four items are in flight there while the producer and the MMA run
-// up to a full ring ahead (into pass 2 while the epilogue waits at the grid
-// barrier).  The merged weight never touches memory; the workspace holds one
-// word per row and two counters, and the last CTA to leave clears it again.
+// items in turn, so four items are in flight there while the producer and the
+// MMA run up to a full ring ahead (into pass 2 while the epilogue waits at the
+// grid barrier).  The merged weight never touches memory.  The workspace holds
+// the barrier's count and generation and two sets of row maxima: a call uses
+// the set of its generation's parity and clears the other one for the next
+// call, so no CTA does clean-up work after its own items.
 // ---------------------------------------------------------------------------
 constexpr int kReqMaxProblems = 16;
 constexpr int kReqGroups = 4;                      // epilogue groups of 4 warps, items taken in turn
@@ -240,10 +243,11 @@ struct ReqBatch {
   ReqProblem p[kReqMaxProblems];
   int count;
   int total_items;
-  int* sync;           // [0] grid barrier, [1] exit ticket; zero on entry, zero again on exit
-  unsigned* rowmax;    // [total rows] |W'| maxima as float bits (non-negative floats order as
-                       // unsigned integers, NaN above +inf); zero on entry, zero again on exit
-  int total_rows;
+  int* sync;           // [0] grid-barrier arrivals (reset by the last arrival), [1] barrier generation
+  unsigned* rowmax;    // [cap_rows][2] |W'| maxima as float bits (non-negative floats order as
+                       // unsigned integers, NaN above +inf), two sets chosen by the generation's
+                       // parity: a call uses one and clears the other for the next call
+  int cap_rows;        // rows the workspace holds
   int b_bytes;         // one B buffer (nbp_max * 16 KB)
   int stage_bytes;     // 16 KB W panel + rp_max*128 B A panel, rounded to 1 KB
   int stages;
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   const int T = batch.total_items;
   int* const gsync = batch.sync;
   unsigned* const rowmax = batch.rowmax;
-  const int total_rows = batch.total_rows;
+  const int cap_rows = batch.cap_rows;
   uint8_t* sB = smem;                                  // 2 x b_bytes
   uint8_t* sRing = smem + batch.off_ring;              // S x stage_bytes
   uint8_t* sQ = smem + batch.off_q;                    // one 2 KB int8 staging buffer per epilogue warp
@@ -324,7 +328,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   uint64_t* final_bar = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_cta = abort_flag + 1;
+  volatile int* s_gen = abort_flag + 1;  // barrier generation seen at entry
   ReqProblem* sp = reinterpret_cast<ReqProblem*>(smem + batch.off_bar + 512);  // problem table
 
   const int warp = threadIdx.x >> 5;
@@ -350,7 +354,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
-    *last_cta = 0;
+    *s_gen = ld_acquire_gpu(&gsync[1]);  // before this CTA arrives: the same value in every CTA
     fence_mbar_init();
   }
   if (warp == 0 && lane < count) {
@@ -460,6 +464,14 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint8_t* buf = sQ + ew * 2048;       // [32 rows x 64 B] int8, 64-byte swizzle
     const int sz = (lane >> 1) & 3;      // chunk c of staging row r sits at c ^ ((r >> 1) & 3)
+    const int gen = *s_gen;
+    const int set = gen & 1;
+    {
+      // clear the other set of row maxima for the next call (nothing reads it in this one)
+      const int r0 = static_cast<int>((static_cast<long long>(cap_rows) * blockIdx.x) / G);
+      const int r1 = static_cast<int>((static_cast<long long>(cap_rows) * (blockIdx.x + 1)) / G);
+      for (int i = r0 + static_cast<int>(threadIdx.x) - 64; i < r1; i += kReqEpiThreads) __stcg(&rowmax[2 * i + (set ^ 1)], 0u);
+    }
     bool bad = false;
     for (int pass = 0; pass < 2; ++pass) {
       if (pass == 1) {
@@ -469,17 +481,22 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         // only the spinning thread knows the outcome: it alone votes, the OR spreads it
         bool grid_failed = false;
         if (ew == 0 && lane == 0) {
-          atomicAdd(&gsync[0], 1);
-          const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
-          const long long t0 = clock64();
-          while (atomicAdd(&gsync[0], 0) < G) {
-            if (clock64() - t0 > limit) {
-              record_timeout(kSiteReqGrid);
-              grid_failed = true;
-              *abort_flag = 1;
-              break;
+          // self-resetting barrier: the last arrival clears the count and opens the next generation
+          if (atomicAdd(&gsync[0], 1) == G - 1) {
+            atomicExch(&gsync[0], 0);
+            __threadfence();
+            atomicAdd(&gsync[1], 1);
+          } else {
+            const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
+            const long long t0 = clock64();
+            while (ld_acquire_gpu(&gsync[1]) == gen) {
+              if (clock64() - t0 > limit) {
+                record_timeout(kSiteReqGrid);
+                grid_failed = true;
+                *abort_flag = 1;
+                break;
+              }
             }
-            __nanosleep(32);
           }
         }
         if (named_bar_any(1, kReqEpiThreads, grid_failed)) bad = true;
@@ -506,10 +523,10 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
           const int grow = sp[w.pi].row0 + n;
           if (pass == 0) {
             // fold the finished row block's maximum into the workspace
-            if (cur_row >= 0) atomicMax(&rowmax[cur_row], req_max_bits(hm));
+            if (cur_row >= 0) atomicMax(&rowmax[2 * cur_row + set], req_max_bits(hm));
             hm = __float2half2_rn(0.0f);
           } else if (n < pn) {
-            const float m = __uint_as_float(__ldcg(&rowmax[grow]));
+            const float m = __uint_as_float(__ldcg(&rowmax[2 * grow + set]));
             scale = scale_from_amax<BW_DTYPE_F16>(m, m != m);
             rcp = __frcp_rn(scale);
             // finite, non-zero scale: every quotient is finite and the packed path applies
@@ -595,22 +612,9 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
 #pragma unroll
         for (int j = 0; j < kReqGroups; ++j) req_walk_next(w, sp, count);
       }
-      if (pass == 0 && !bad && cur_row >= 0) atomicMax(&rowmax[cur_row], req_max_bits(hm));
+      if (pass == 0 && !bad && cur_row >= 0) atomicMax(&rowmax[2 * cur_row + set], req_max_bits(hm));
     }
     if (lane == 0) tma_store_wait0();
-    // ---- exit: the last CTA out clears the workspace for the next call ----
-    __threadfence();
-    named_bar_sync(1, kReqEpiThreads);
-    if (ew == 0 && lane == 0) *last_cta = atomicAdd(&gsync[1], 1) == G - 1 ? 1 : 0;
-    named_bar_sync(1, kReqEpiThreads);
-    if (*last_cta) {
-      __threadfence();
-      for (int i = threadIdx.x - 64; i < total_rows; i += kReqEpiThreads) __stcg(&rowmax[i], 0u);
-      if (ew == 0 && lane == 0) {
-        atomicExch(&gsync[0], 0);
-        atomicExch(&gsync[1], 0);
-      }
-    }
   }
 
   tc_fence_before();
@@ -758,8 +762,8 @@ static bool req_tc_eligible(const bw_lora_requant_problem& P) {
 // Items (128-row x 64-column panels) of one problem.
 static int64_t req_items(const bw_lora_requant_problem& P) { return ((P.n + 127) / 128) * ((P.k + 63) / 64); }
 
-// Two counters, then one word per row of the launch.
-static size_t req_workspace_bytes(int64_t rows) { return 256 + static_cast<size_t>(rows) * sizeof(unsigned); }
+// Barrier count and generation, then two words per row of the launch.
+static size_t req_workspace_bytes(int64_t rows) { return 256 + static_cast<size_t>(rows) * 2 * sizeof(unsigned); }
 
 struct ReqPlan {
   int smem = 0, stages = 0;
@@ -826,7 +830,7 @@ static int launch_req_coop(const bw_lora_requant_problem* probs, const int* idx,
     return fail(BW_ERR_WORKSPACE, "lora_merge_requant: workspace of %zu bytes (256-byte aligned) required, %zu given",
                 need, ws_bytes);
   b.total_items = static_cast<int>(items);
-  b.total_rows = static_cast<int>(rows);
+  b.cap_rows = static_cast<int>(std::min<size_t>((ws_bytes - 256) / (2 * sizeof(unsigned)), size_t(1) << 30));
   b.sync = static_cast<int*>(workspace);
   b.rowmax = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) + 256);
   const ReqPlan pl = req_plan(rp_max);

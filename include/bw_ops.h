@@ -122,10 +122,12 @@ int bw_lora_merge(const void* w, int64_t ldw, const void* a, const void* b, floa
  * Fused delta + merge + per-channel requantisation of the merged weight:
  * (q, scale) = quantize_weight_int8(add_delta(w, lora_delta(a, b, scaling))).
  * The merged fp16 weight is never written to memory.  q [n, k] int8 row stride
- * ldq; scale [n] fp16.  Workspace: bw_lora_merge_requant_workspace_size() bytes
- * (two counters and one word per row), 256-byte aligned, zero before its first
- * use; every call that completes leaves it zero again (after a device timeout,
- * zero it again).  Calls sharing a workspace must not overlap on the GPU.
+ * ldq; scale [n] fp16.  Workspace: at least bw_lora_merge_requant_workspace_size()
+ * bytes (a grid-barrier count and generation, then two words per row),
+ * 256-byte aligned, zero before its first use, and always passed with the same
+ * workspace_bytes (its full size): each call clears the half the next call
+ * uses, over that size.  After a device timeout, zero it again.  Calls sharing
+ * a workspace must not overlap on the GPU.
  * Composes lora_ops.cu:16-38 and int8_gemm.py:63-68.
  */
 size_t bw_lora_merge_requant_workspace_size(int64_t n, int64_t k, int64_t r);

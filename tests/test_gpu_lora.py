@@ -199,18 +199,19 @@ def test_lora_merge_requant_special_rows(cuda_dev, ops):
 
 
 def test_lora_merge_requant_many_problems_reuse_workspace(cuda_dev, ops):
-    """More than 16 problems: several launches in a row share one workspace, which each leaves zeroed."""
+    """More than 16 problems: several launches in a row share one workspace.
+
+    Each launch uses the row-maxima set of its barrier generation's parity and
+    clears the other; three rounds of two launches reuse each set several times.
+    """
     cuda, _ = ops
     specs = [(16 if i % 2 else 64, 128 * (1 + i % 3), 64 * (2 + i % 5)) for i in range(21)]
     items = []
     for i, (r, n, k) in enumerate(specs):
         A, B, W = make(800 + i, r, n, k)
         items.append((dev16(W, cuda_dev), dev16(A, cuda_dev), dev16(B, cuda_dev), 1.5))
-    for _ in range(2):
+    for _ in range(3):
         outs = cuda.lora_merge_requant_batched(items)
         for (W, A, B, s), (q, sc) in zip(items, outs):
             qm, sm = quant.quantize_weight_int8(cuda.lora_merge(W, A, B, s).cpu().numpy(), F16)
             assert np.array_equal(q.cpu().numpy(), qm) and np.array_equal(sc.cpu().numpy(), sm)
-    torch.cuda.synchronize()
-    for ws in cuda._ws.values():
-        assert int(ws.count_nonzero()) == 0
