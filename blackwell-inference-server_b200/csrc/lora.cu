@@ -296,6 +296,29 @@ __device__ __forceinline__ void req_walk_next(ReqWalk& w, const ReqProblem* sp, 
   }
 }
 
+// 32 merged values of a row and their 32 codes.
+struct ReqHalfRow {
+  __half2 v[16];
+};
+struct ReqCodes {
+  uint32_t w[8];
+};
+
+// Codes of a row whose scale is not a normal fp16 number: subnormal (packed
+// quantiser with its clamp) or zero / inf / NaN (closed form).  Out of line:
+// such rows are rare and the hot loop stays small.
+static __device__ __noinline__ ReqCodes req_codes_rare(ReqHalfRow m, float scale, float rcp, bool fast_row) {
+  ReqCodes q;
+  if (fast_row) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q.w[e] = quant4_f16<true>(m.v[2 * e], m.v[2 * e + 1], scale, rcp);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q.w[e] = quant4_special(m.v[2 * e], m.v[2 * e + 1], scale);
+  }
+  return q;
+}
+
 // |W'| maximum of a half2 running max as float bits, NaN if either half is NaN.
 __device__ __forceinline__ unsigned req_max_bits(__half2 hm) {
   const float l = __low2float(hm), h = __high2float(hm);
@@ -483,9 +506,9 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         if (ew == 0 && lane == 0) {
           // self-resetting barrier: the last arrival clears the count and opens the next generation
           if (atomicAdd(&gsync[0], 1) == G - 1) {
-            atomicExch(&gsync[0], 0);
             __threadfence();
-            atomicAdd(&gsync[1], 1);
+            atomicAdd(&gsync[1], 1);   // open the waiters first
+            atomicExch(&gsync[0], 0);  // the count is next needed by the next call
           } else {
             const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
             const long long t0 = clock64();
@@ -552,7 +575,8 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
           __syncwarp();
         }
         // two 32-column halves: half the registers of a 64-column pass, so four groups fit
-#pragma unroll
+        // (not unrolled: a smaller loop body keeps the instruction cache and registers in reach)
+#pragma unroll 1
         for (int h = 0; h < 2; ++h) {
           uint32_t acc[32];
           tmem_ld32(lane_addr + d * 64 + h * 32, acc);
@@ -574,9 +598,10 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             const uint32_t* w32 = reinterpret_cast<const uint32_t*>(&wv[c]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const __half2 dl = __floats2half2_rn(__uint_as_float(acc[8 * c + 2 * e]) * s,
-                                                   __uint_as_float(acc[8 * c + 2 * e + 1]) * s);
-              merged[4 * c + e] = __hadd2(*reinterpret_cast<const __half2*>(&w32[e]), dl);
+              const float2 p = __fmul2_rn(make_float2(__uint_as_float(acc[8 * c + 2 * e]),
+                                                      __uint_as_float(acc[8 * c + 2 * e + 1])),
+                                          make_float2(s, s));
+              merged[4 * c + e] = __hadd2(*reinterpret_cast<const __half2*>(&w32[e]), __float22half2_rn(p));
             }
           }
           if (pass == 0) {
@@ -584,21 +609,17 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             for (int e = 0; e < 16; ++e) hm = __hmax2_nan(hm, __habs2(merged[e]));
             continue;
           }
-          uint32_t qw[8];
+          ReqCodes qw;
           if (normal_row) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) qw[e] = quant4_f16<false>(merged[2 * e], merged[2 * e + 1], scale, rcp);
-          } else if (fast_row) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qw[e] = quant4_f16<true>(merged[2 * e], merged[2 * e + 1], scale, rcp);
+            for (int e = 0; e < 8; ++e) qw.w[e] = quant4_f16<false>(merged[2 * e], merged[2 * e + 1], scale, rcp);
           } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qw[e] = quant4_special(merged[2 * e], merged[2 * e + 1], scale);
+            qw = req_codes_rare(*reinterpret_cast<const ReqHalfRow*>(merged), scale, rcp, fast_row);
           }
 #pragma unroll
           for (int c = 0; c < 2; ++c)
             *reinterpret_cast<uint4*>(buf + lane * 64 + (((2 * h + c) ^ sz) << 4)) =
-                make_uint4(qw[4 * c], qw[4 * c + 1], qw[4 * c + 2], qw[4 * c + 3]);
+                make_uint4(qw.w[4 * c], qw.w[4 * c + 1], qw.w[4 * c + 2], qw.w[4 * c + 3]);
         }
         if (pass == 1) {
           fence_proxy_async_smem();

@@ -115,9 +115,10 @@ static __device__ __noinline__ uint32_t quant4_fix(uint32_t packed, __half2 w01,
 // +-127.0625 and the rounding lands on codes -127..127 without the clamp.
 template <bool CLAMP = true>
 __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s, float rcp) {
-  const float2 f01 = __half22float2(w01);
-  const float2 f23 = __half22float2(w23);
-  const float x[4] = {__fmul_rn(f01.x, rcp), __fmul_rn(f01.y, rcp), __fmul_rn(f23.x, rcp), __fmul_rn(f23.y, rcp)};
+  // packed fp32 multiplies: each lane is the IEEE round-to-nearest product
+  const float2 x01 = __fmul2_rn(__half22float2(w01), make_float2(rcp, rcp));
+  const float2 x23 = __fmul2_rn(__half22float2(w23), make_float2(rcp, rcp));
+  const float x[4] = {x01.x, x01.y, x23.x, x23.y};
   const __half2 bias = __float2half2_rn(1536.0f);
   __half2 y01 = __floats2half2_rn(x[0], x[1]);
   __half2 y23 = __floats2half2_rn(x[2], x[3]);
