@@ -337,7 +337,7 @@ struct PCfg {
   static_assert(BM >= 16 && BM <= 128 && BM % 16 == 0, "UMMA N for M=128");
   static_assert(D_COL0 + 2 * BM <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert((2 * STAGES + 2 * ASTAGES + 4 + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
+  static_assert((3 * STAGES + 2 * ASTAGES + 4 + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
 };
 
 enum PersistentWaitSite : int {
@@ -372,7 +372,8 @@ __global__ void __launch_bounds__(448, 1)
   uint64_t* dfull = aempty + ASTAGES;    // 2
   uint64_t* dempty = dfull + 2;          // 2
   uint64_t* final_bar = dempty + 2;      // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  uint64_t* xfull = final_bar + 1;       // STAGES: the x tiles of a stage (full[] covers its W tile)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket = abort_flag + 1;
 
@@ -382,6 +383,7 @@ __global__ void __launch_bounds__(448, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&xfull[s], 1);
       mbar_init(&empty[s], 4 + 1);  // one group of 4 dequantiser warps + 1 MMA commit
     }
     for (int t = 0; t < ASTAGES; ++t) {
@@ -433,7 +435,7 @@ __global__ void __launch_bounds__(448, 1)
         while (uu < units && pre < STAGES) {
           int nt, mt, kb0, nkb;
           unit_kb(uu, nt, mt, kb0, nkb);
-          mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[pre], C::W_BYTES);
           tma_load_2d(sW + pre * C::W_BYTES, &tm_w, &full[pre], (kb0 + ii) * C::BK, nt * 128, pol_w);
           ++pre;
           if (++ii == nkb) {
@@ -456,11 +458,12 @@ __global__ void __launch_bounds__(448, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[s], C::W_BYTES);
           tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], kx, nt * 128, pol_w);
         }
-        tma_load_2d(sX + s * C::X_BYTES, &tm_x, &full[s], kx, mt * BM, pol_x);
-        tma_load_2d(sX + s * C::X_BYTES + C::X_PANEL, &tm_x, &full[s], kx + 64, mt * BM, pol_x);
+        mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
+        tma_load_2d(sX + s * C::X_BYTES, &tm_x, &xfull[s], kx, mt * BM, pol_x);
+        tma_load_2d(sX + s * C::X_BYTES + C::X_PANEL, &tm_x, &xfull[s], kx + 64, mt * BM, pol_x);
         ++it;
         if (++i == nkb) {
           i = 0;
@@ -469,7 +472,10 @@ __global__ void __launch_bounds__(448, 1)
       }
       if (!ok) {
         for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+        {
           mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
+          mbar_wait(&xfull[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
+        }
       }
     }
   } else if (warp == 1) {
@@ -491,7 +497,7 @@ __global__ void __launch_bounds__(448, 1)
           const uint32_t ph = (it / STAGES) & 1;
           const int t = it % ASTAGES;
           const uint32_t pa = (it / ASTAGES) & 1;
-          if (!mbar_wait(&afull[t], pa, abort_flag, kSitePMmaA) || !mbar_wait(&full[s], ph, abort_flag, kSitePMmaFull)) {
+          if (!mbar_wait(&afull[t], pa, abort_flag, kSitePMmaA) || !mbar_wait(&xfull[s], ph, abort_flag, kSitePMmaFull)) {
             ok = false;
             break;
           }
@@ -631,21 +637,37 @@ __global__ void __launch_bounds__(448, 1)
           __threadfence();
           const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
           const float* base = ws + static_cast<size_t>(t) * splits * (128 * BM) + static_cast<size_t>(row) * BM;
-          for (int c0 = 0; c0 < BM; c0 += 4) {
-            float4 acc = __ldcg(reinterpret_cast<const float4*>(base + c0));
-            for (int p = 1; p < splits; ++p) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(base + static_cast<size_t>(p) * 128 * BM + c0));
-              acc.x += v.x;
-              acc.y += v.y;
-              acc.z += v.z;
-              acc.w += v.w;
+          // 8 columns at a time; the loads of four partials are issued together, then
+          // summed in split order (partial 0 first, as the result must not depend on timing)
+#pragma unroll 1
+          for (int c0 = 0; c0 < BM; c0 += 8) {
+            float a[8];
+#pragma unroll 1
+            for (int p0 = 0; p0 < splits; p0 += 4) {
+              float4 v[4][2];
+#pragma unroll
+              for (int pp = 0; pp < 4; ++pp)
+#pragma unroll
+                for (int e = 0; e < 2; ++e)
+                  v[pp][e] = p0 + pp < splits ? __ldcg(reinterpret_cast<const float4*>(
+                                                    base + static_cast<size_t>(p0 + pp) * 128 * BM + c0 + 4 * e))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int pp = 0; pp < 4; ++pp) {
+                if (p0 + pp >= splits) break;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const float f[4] = {v[pp][e].x, v[pp][e].y, v[pp][e].z, v[pp][e].w};
+#pragma unroll
+                  for (int g = 0; g < 4; ++g) a[4 * e + g] = (p0 + pp == 0) ? f[g] : a[4 * e + g] + f[g];
+                }
+              }
             }
             if (n < N) {
-              const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
+              for (int e = 0; e < 8; ++e) {
                 const int m = m0 + c0 + e;
-                if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, a4[e] * sc);
+                if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, a[e] * sc);
               }
             }
           }
