@@ -258,8 +258,6 @@ class MergeRequantWorkload:
 class GemmSweepWorkload:
     """cfg1 / cfg3 / cfg4: W8A16 GEMMs through bw_w8a16_gemm on resident weights."""
 
-    kernel = "w8a16_tc_kernel"
-
     def __init__(self, name, dev, rank, world, m):
         from blackwell_ops import _lib
 
@@ -267,6 +265,8 @@ class GemmSweepWorkload:
         self.dev = dev
         self.name = name
         self.m = m
+        # M <= 128 runs the persistent kernel, larger M the one-tile-per-CTA kernel
+        self.kernel = "w8a16_persistent_kernel" if m <= 128 else "w8a16_tc_kernel"
         g = torch.Generator(device=dev).manual_seed(2000 + rank)
         if name == "cfg1":
             shapes = [(1024, 3072)] * 64
