@@ -1,6 +1,6 @@
 // Shared device/host helpers for the sm_100a W8A16 / LoRA-delta kernels.
 //
-// * PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor, no multicast),
+// * PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor; every CTA loads its own tiles),
 //   and the 5th-generation tensor core (tcgen05.mma / TMEM).
 // * Bounded waits: every spin on an mbarrier gives up after BW_WAIT_LIMIT_NS,
 //   records a site id in the device status word and lets the caller unwind,
@@ -99,7 +99,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---------------------------------------------------------------------------
-// thread-block clusters: distributed shared memory (no TMA multicast anywhere)
+// thread-block clusters: distributed shared memory (every CTA loads its own TMA tiles)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -190,6 +190,11 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {

@@ -110,8 +110,9 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x;
-  const int m_tile = blockIdx.y;
+  // M-tile fastest: the CTAs that share a weight tile are launched side by side and read it once
+  const int m_tile = blockIdx.x;
+  const int n_tile = blockIdx.y;
   const int split = blockIdx.z;
   const int n0 = n_tile * 128;
   const int m0 = m_tile * BM;
@@ -146,7 +147,8 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
+      // a weight tile read by several M-tiles stays in L2 for its neighbours; read once, it streams
+      const uint64_t pol_w = gridDim.x > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       int issued = 0;
       for (int i = 0; i < nkb; ++i) {
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       } else {
-        const int tile = m_tile * gridDim.x + n_tile;
+        const int tile = m_tile * gridDim.y + n_tile;
         float* mine = ws + (static_cast<size_t>(tile) * splits + split) * (128 * BM) + static_cast<size_t>(row) * BM;
 #pragma unroll
         for (int c0 = 0; c0 < BM; c0 += 16) {
@@ -803,7 +805,7 @@ static int launch_tc(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap
     attr_err = cudaFuncSetAttribute(w8a16_tc_kernel<BM, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   });
   if (int s = check_cuda(attr_err, "cudaFuncSetAttribute(w8a16_tc_kernel)")) return s;
-  dim3 grid(p.n_tiles, p.m_tiles, p.splits);
+  dim3 grid(p.m_tiles, p.n_tiles, p.splits);
   w8a16_tc_kernel<BM, BF16><<<grid, 192, C::SMEM, st>>>(tw, tx, scale, sdt, y, ldy, M, N, p.kblocks,
                                                           p.kb_per_split, p.splits, ws, counters);
   return check_launch("w8a16_tc_kernel");
