@@ -809,7 +809,9 @@ def main():
         cpu = {"value": round(scale_unit(tot, secs, wl.metric_kind), 6), "unit": wl.unit,
                "cores": torch.get_num_threads(), "kind": "port", "sample": desc + f", {i - 1} samples"}
 
-    graphs.clear()  # graphs holding NCCL work are released before the process group
+    for g in graphs:  # graphs holding NCCL work are released before the process group
+        g.reset()
+    graphs.clear()
     torch.cuda.synchronize()
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 4), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
@@ -821,7 +823,20 @@ def main():
                 "clocks": sampler.summary(), "device_status": status}
         print(json.dumps(line), flush=True)
     if world > 1:
+        # the result is out; bound the teardown so a stuck communicator cannot hold the GPUs
+        import threading
+
+        def _bail():
+            sys.stdout.flush()
+            sys.stderr.flush()
+            os._exit(0)
+
+        guard = threading.Timer(60.0, _bail)
+        guard.daemon = True
+        guard.start()
+        barrier()
         dist.destroy_process_group()
+        guard.cancel()
 
 
 if __name__ == "__main__":

@@ -17,6 +17,9 @@
 // kernel that re-reads the row (from L2) instead.
 #include <stdio.h>
 
+#include <algorithm>
+#include <mutex>
+
 #include "quant_math.cuh"
 
 namespace bw {
@@ -147,6 +150,138 @@ __global__ void __launch_bounds__(512) quantize_rows_reg_kernel(const uint8_t* _
   }
 }
 
+// Streaming kernel for aligned rows of up to a few tens of KB: one or two CTAs
+// per SM walk rows blockIdx.x, + gridDim.x, ...; thread 0 keeps `stages` rows in
+// flight with 1-D bulk copies into a shared-memory ring, and all 256 threads
+// reduce |w| and write the codes of the current row from shared memory.  The
+// arithmetic is the register kernel's (fp16 rows with a normal scale use the
+// packed quantiser, proved equal to it).
+constexpr int kQsThreads = 256;
+constexpr int kQsMaxStages = 8;
+enum QuantWaitSite : int { kSiteQsFull = 301 };
+
+template <int DT>
+__global__ void __launch_bounds__(kQsThreads) quantize_rows_stream_kernel(const uint8_t* __restrict__ w,
+                                                                        int64_t ldw_bytes, int64_t n, int64_t k,
+                                                                        int8_t* __restrict__ q, int64_t ldq,
+                                                                        void* __restrict__ scale, int stage_bytes,
+                                                                        int stages) {
+  constexpr int EB = kElemBytes[DT];
+  constexpr int E = 16 / EB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(stages) * stage_bytes);
+  __shared__ float red[kQsThreads / 32];
+  __shared__ int redn[kQsThreads / 32];
+  __shared__ int abort_flag_s;
+  volatile int* abort_flag = &abort_flag_s;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const uint32_t row_bytes = static_cast<uint32_t>(k * EB);
+  const int nchunks = static_cast<int>(row_bytes / 16);
+  const int64_t G = gridDim.x;
+  const int64_t mine = n > blockIdx.x ? (n - blockIdx.x + G - 1) / G : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    abort_flag_s = 0;
+    fence_mbar_init();
+    const uint64_t once = l2_policy_evict_first();
+    for (int64_t i = 0; i < mine && i < stages; ++i) {
+      const int64_t row = blockIdx.x + i * G;
+      mbar_arrive_expect_tx(&full[i], row_bytes);
+      bulk_load_1d(ring + i * stage_bytes, w + row * ldw_bytes, row_bytes, &full[i], once);
+    }
+  }
+  __syncthreads();
+  const uint64_t once = l2_policy_evict_first();
+  int64_t i = 0;
+  for (; i < mine; ++i) {
+    const int st = static_cast<int>(i % stages);
+    const int64_t row = blockIdx.x + i * G;
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>((i / stages) & 1), abort_flag, kSiteQsFull);
+    if (__syncthreads_or(!ok)) break;  // one decision for the block
+    const uint4* src = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(st) * stage_bytes);
+    // pass 1: row maximum of |w| (NaN-propagating flag)
+    float amax = 0.f;
+    bool nan = false;
+    for (int c = tid; c < nchunks; c += kQsThreads) {
+      float f[E];
+      chunk_values<DT>(src[c], f);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        nan |= (f[e] != f[e]);
+        amax = fmaxf(amax, fabsf(f[e]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    nan = __any_sync(0xffffffffu, nan);
+    if (lane == 0) {
+      red[warp] = amax;
+      redn[warp] = nan ? 1 : 0;
+    }
+    __syncthreads();
+    amax = 0.f;
+    nan = false;
+#pragma unroll
+    for (int j = 0; j < kQsThreads / 32; ++j) {
+      amax = fmaxf(amax, red[j]);
+      nan |= redn[j] != 0;
+    }
+    const float s = scale_from_amax<DT>(amax, nan);
+    const float rcp = __frcp_rn(s);
+    if (tid == 0) store_scale<DT>(scale, row, s);
+    // pass 2: codes
+    int8_t* qr = q + row * ldq;
+    if constexpr (DT == BW_DTYPE_F16) {
+      if (s >= 6.103515625e-05f && s < __int_as_float(0x7f800000)) {  // normal scale: packed, clamp-free
+        for (int c = tid; c < nchunks; c += kQsThreads) {
+          const uint4 v = src[c];
+          const __half2* h = reinterpret_cast<const __half2*>(&v);
+          uint2 o;
+          o.x = quant4_f16<false>(h[0], h[1], s, rcp);
+          o.y = quant4_f16<false>(h[2], h[3], s, rcp);
+          *reinterpret_cast<uint2*>(qr + c * 8) = o;
+        }
+      } else {
+        for (int c = tid; c < nchunks; c += kQsThreads) {
+          float f[E];
+          chunk_values<DT>(src[c], f);
+          int8_t out[E];
+#pragma unroll
+          for (int e = 0; e < E; ++e) out[e] = quant_fast<DT>(f[e], s, rcp);
+          *reinterpret_cast<uint2*>(qr + c * E) = *reinterpret_cast<uint2*>(out);
+        }
+      }
+    } else {
+      for (int c = tid; c < nchunks; c += kQsThreads) {
+        float f[E];
+        chunk_values<DT>(src[c], f);
+        int8_t out[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) out[e] = quant_fast<DT>(f[e], s, rcp);
+        if constexpr (E == 8) *reinterpret_cast<uint2*>(qr + c * E) = *reinterpret_cast<uint2*>(out);
+        else *reinterpret_cast<uint32_t*>(qr + c * E) = *reinterpret_cast<uint32_t*>(out);
+      }
+    }
+    __syncthreads();  // every thread is done with this stage and with red[]
+    if (tid == 0 && i + stages < mine) {
+      const int64_t nrow = blockIdx.x + (i + stages) * G;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&full[st], row_bytes);
+      bulk_load_1d(ring + static_cast<size_t>(st) * stage_bytes, w + nrow * ldw_bytes, row_bytes, &full[st], once);
+    }
+  }
+  if (i < mine && tid == 0) {
+    // a wait gave up: let the copies still in flight land before this CTA's shared memory is released
+    const int64_t issued = mine < i + stages ? mine : i + stages;
+    for (int64_t j = i; j < issued; ++j)
+      mbar_wait(&full[j % stages], static_cast<uint32_t>((j / stages) & 1), nullptr, kSiteQsFull);
+  }
+}
+
 // Any layout, any length: one block of 256 threads per row, two passes.
 template <int DT>
 __global__ void __launch_bounds__(256) quantize_rows_generic_kernel(const uint8_t* __restrict__ w, int64_t ldw_bytes,
@@ -183,6 +318,45 @@ static void launch_reg(const void* w, int64_t ldw_bytes, int64_t n, int64_t k, i
       static_cast<const uint8_t*>(w), ldw_bytes, n, k, q, ldq, scale, group);
 }
 
+// Streaming plan: stage size and count, CTAs per SM; false if the rows do not suit it.
+struct QsPlan {
+  int stage_bytes = 0, stages = 0, per_sm = 0, smem = 0;
+};
+static bool qs_plan(int64_t row_bytes, QsPlan& p) {
+  if (row_bytes % 16 != 0 || row_bytes > 96 * 1024) return false;
+  p.stage_bytes = static_cast<int>((row_bytes + 127) / 128 * 128);
+  for (int cps = 2; cps >= 1; --cps) {
+    const int budget = (cps == 2 ? 112 : 224) * 1024;
+    const int s = std::min(kQsMaxStages, (budget - 256) / p.stage_bytes);
+    if (s >= 3 || (cps == 1 && s >= 2)) {
+      p.stages = s;
+      p.per_sm = cps;
+      p.smem = s * p.stage_bytes + s * 8 + 128;
+      return true;
+    }
+  }
+  return false;
+}
+
+template <int DT>
+static int launch_stream(const void* w, int64_t ldw_bytes, int64_t n, int64_t k, int8_t* q, int64_t ldq, void* scale,
+                         const QsPlan& p, cudaStream_t st) {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    // the kernel's static shared memory (reduction scratch) comes out of the same 227 KB
+    err[dev & 63] = cudaFuncSetAttribute(quantize_rows_stream_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         226 * 1024);
+  });
+  if (int s = check_cuda(err[dev & 63], "cudaFuncSetAttribute(quantize_rows_stream_kernel)")) return s;
+  const int64_t grid = std::min<int64_t>(n, static_cast<int64_t>(p.per_sm) * num_sms());
+  quantize_rows_stream_kernel<DT><<<static_cast<unsigned>(grid), kQsThreads, p.smem, st>>>(
+      static_cast<const uint8_t*>(w), ldw_bytes, n, k, q, ldq, scale, p.stage_bytes, p.stages);
+  return check_launch("quantize_rows_stream_kernel");
+}
+
 template <int DT>
 static int quantize_dispatch(const void* w, int64_t n, int64_t k, int64_t ldw, int8_t* q, int64_t ldq,
                              void* scale, cudaStream_t st) {
@@ -191,6 +365,8 @@ static int quantize_dispatch(const void* w, int64_t n, int64_t k, int64_t ldw, i
   const int64_t ldw_bytes = ldw * EB;
   const bool aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (ldw_bytes % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (ldq % 16 == 0);
+  QsPlan qp;
+  if (aligned && n >= 2 * num_sms() && qs_plan(k * EB, qp)) return launch_stream<DT>(w, ldw_bytes, n, k, q, ldq, scale, qp, st);
   const int64_t nchunks = (k + E - 1) / E;
   int group = 32;
   while (group < 512 && (nchunks + group - 1) / group > 8) group <<= 1;

@@ -85,8 +85,10 @@ def _worker(rank, world, port, cases, out_dir):
                 tol = 1e-2 if dt == "f16" else 1e-2 + 2 ** -8 * float(ref32.abs().max())
                 assert float((y.float() - ref32).abs().max()) <= tol
                 assert float((y.float() - ref32).norm() / ref32.norm()) <= (1e-3 if dt == "f16" else 4e-3)
+                # the unsplit GEMM may pick another split-K plan: one output ulp apart at most
                 y1 = int8_gemm(x, q_full, s_full)
-                assert float((y.float() - y1.float()).abs().max()) <= 1e-2
+                ulp = 2.0 ** (-10 if dt == "f16" else -7) * y1.float().abs() + 2.0 ** -24
+                assert bool(((y.float() - y1.float()).abs() <= ulp).all())
             except Exception as e:
                 failures.append(f"case {(m, n, k, dt)} check: {type(e).__name__}: {e}")
     if _lib.device_status() != 0:
