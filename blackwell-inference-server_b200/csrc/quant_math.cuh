@@ -140,6 +140,48 @@ __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s
   return packed;
 }
 
+// bf16 counterpart of quant4_f16, for a row whose scale is finite, non-zero and
+// has a finite reciprocal: x = RN32(w * rcp) rounded to bf16 in packed form,
+// clamped to +-127 in bf16, rounded to an integer by adding 1.5 * 2^23 in fp32
+// (spacing 1 there, so the add is round-to-nearest-even) and the code is the low
+// byte of the sum.  x within 4 fp32 ulps (low 16 bits) of a bf16 rounding
+// midpoint takes the exact division.  Checked against quant_one<bf16> for every
+// finite bf16 weight and every such scale.
+static __device__ __noinline__ uint32_t quant4_bf16_fix(uint32_t packed, __nv_bfloat162 w01, __nv_bfloat162 w23,
+                                                        float s, float rcp) {
+  const float f[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (((__float_as_uint(__fmul_rn(f[e], rcp)) + 4u) & 0xFFF8u) == 0x8000u) {
+      const uint32_t code = static_cast<uint8_t>(quant_one<BW_DTYPE_BF16>(f[e], s));
+      packed = (packed & ~(0xFFu << (8 * e))) | (code << (8 * e));
+    }
+  }
+  return packed;
+}
+
+__device__ __forceinline__ uint32_t quant4_bf16(__nv_bfloat162 w01, __nv_bfloat162 w23, float s, float rcp) {
+  const float2 x01 = __fmul2_rn(__bfloat1622float2(w01), make_float2(rcp, rcp));
+  const float2 x23 = __fmul2_rn(__bfloat1622float2(w23), make_float2(rcp, rcp));
+  const __nv_bfloat162 lim = __float2bfloat162_rn(127.0f);
+  const __nv_bfloat162 nlim = __float2bfloat162_rn(-127.0f);
+  const __nv_bfloat162 y01 = __hmin2(__hmax2(__float22bfloat162_rn(x01), nlim), lim);
+  const __nv_bfloat162 y23 = __hmin2(__hmax2(__float22bfloat162_rn(x23), nlim), lim);
+  const float2 m = make_float2(12582912.0f, 12582912.0f);
+  const float2 z01 = __fadd2_rn(__bfloat1622float2(y01), m);
+  const float2 z23 = __fadd2_rn(__bfloat1622float2(y23), m);
+  uint32_t t01, t23, packed;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(t01) : "r"(__float_as_uint(z01.x)), "r"(__float_as_uint(z01.y)));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(t23) : "r"(__float_as_uint(z23.x)), "r"(__float_as_uint(z23.y)));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(packed) : "r"(t01), "r"(t23));
+  const bool near = ((((__float_as_uint(x01.x) + 4u) & 0xFFF8u) == 0x8000u) |
+                     (((__float_as_uint(x01.y) + 4u) & 0xFFF8u) == 0x8000u) |
+                     (((__float_as_uint(x23.x) + 4u) & 0xFFF8u) == 0x8000u) |
+                     (((__float_as_uint(x23.y) + 4u) & 0xFFF8u) == 0x8000u));
+  if (near) packed = quant4_bf16_fix(packed, w01, w23, s, rcp);
+  return packed;
+}
+
 // quant_one<fp16>'s codes, four at a time, for a row whose scale is not a
 // finite positive number, in closed form: a NaN or +inf scale gives 0 for
 // every element (w / inf = 0, inf / inf = NaN -> 0); a zero scale (a row of

@@ -18,6 +18,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <mutex>
 
 #include "quant_math.cuh"
@@ -206,14 +207,30 @@ __global__ void __launch_bounds__(kQsThreads) quantize_rows_stream_kernel(const 
     // pass 1: row maximum of |w| (NaN-propagating flag)
     float amax = 0.f;
     bool nan = false;
-    for (int c = tid; c < nchunks; c += kQsThreads) {
-      float f[E];
-      chunk_values<DT>(src[c], f);
+    if constexpr (DT == BW_DTYPE_F32) {
+      for (int c = tid; c < nchunks; c += kQsThreads) {
+        float f[E];
+        chunk_values<DT>(src[c], f);
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        nan |= (f[e] != f[e]);
-        amax = fmaxf(amax, fabsf(f[e]));
+        for (int e = 0; e < E; ++e) {
+          nan |= (f[e] != f[e]);
+          amax = fmaxf(amax, fabsf(f[e]));
+        }
       }
+    } else {
+      // packed |w| maxima in the weight dtype (exact), NaN carried by the _nan max
+      using T2 = typename std::conditional<DT == BW_DTYPE_F16, __half2, __nv_bfloat162>::type;
+      T2 hm;
+      *reinterpret_cast<uint32_t*>(&hm) = 0u;  // +0, +0
+      for (int c = tid; c < nchunks; c += kQsThreads) {
+        const uint4 v = src[c];
+        const T2* h = reinterpret_cast<const T2*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hm = __hmax2_nan(hm, __habs2(h[e]));
+      }
+      const float l = __low2float(hm), hh = __high2float(hm);
+      nan = (l != l) || (hh != hh);
+      amax = nan ? 0.f : fmaxf(l, hh);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -255,6 +272,26 @@ __global__ void __launch_bounds__(kQsThreads) quantize_rows_stream_kernel(const 
           *reinterpret_cast<uint2*>(qr + c * E) = *reinterpret_cast<uint2*>(out);
         }
       }
+    } else if constexpr (DT == BW_DTYPE_BF16) {
+      if (s > 0.0f && s < __int_as_float(0x7f800000) && rcp < 1.0e30f) {  // packed quantiser
+        for (int c = tid; c < nchunks; c += kQsThreads) {
+          const uint4 v = src[c];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+          uint2 o;
+          o.x = quant4_bf16(h[0], h[1], s, rcp);
+          o.y = quant4_bf16(h[2], h[3], s, rcp);
+          *reinterpret_cast<uint2*>(qr + c * 8) = o;
+        }
+      } else {
+        for (int c = tid; c < nchunks; c += kQsThreads) {
+          float f[E];
+          chunk_values<DT>(src[c], f);
+          int8_t out[E];
+#pragma unroll
+          for (int e = 0; e < E; ++e) out[e] = quant_fast<DT>(f[e], s, rcp);
+          *reinterpret_cast<uint2*>(qr + c * E) = *reinterpret_cast<uint2*>(out);
+        }
+      }
     } else {
       for (int c = tid; c < nchunks; c += kQsThreads) {
         float f[E];
@@ -262,8 +299,7 @@ __global__ void __launch_bounds__(kQsThreads) quantize_rows_stream_kernel(const 
         int8_t out[E];
 #pragma unroll
         for (int e = 0; e < E; ++e) out[e] = quant_fast<DT>(f[e], s, rcp);
-        if constexpr (E == 8) *reinterpret_cast<uint2*>(qr + c * E) = *reinterpret_cast<uint2*>(out);
-        else *reinterpret_cast<uint32_t*>(qr + c * E) = *reinterpret_cast<uint32_t*>(out);
+        *reinterpret_cast<uint32_t*>(qr + c * E) = *reinterpret_cast<uint32_t*>(out);
       }
     }
     __syncthreads();  // every thread is done with this stage and with red[]

@@ -9,7 +9,7 @@
 // arithmetic is IEEE single precision; build without fast-math or FP
 // contraction.
 //
-// usage: quant_fast_check f16|bf16|f32|f16packed|f16packed_noclamp [scale_stride]
+// usage: quant_fast_check f16|bf16|f32|f16packed|f16packed_noclamp|bf16packed [scale_stride]
 //   -> prints "mismatches=<n> slow=<n> total=<n>"; scale_stride > 1 checks every
 //   stride-th scale (all weights) to bound the run time.
 #include <cmath>
@@ -146,6 +146,54 @@ static void run_packed_noclamp(int stride) {
   std::printf("mismatches=%ld slow=%ld total=%ld\n", m, sl, tot);
 }
 
+// Emulation of quant4_bf16 (csrc/quant_math.cuh) for one element: x = RN32(w*rcp)
+// rounded to bf16, clamped to +-127 in bf16, rounded to an integer by adding
+// 1.5*2^23 in fp32 (spacing 1 there: round-to-nearest-even), code = low byte of
+// the sum's bits; exact path when x's low 16 bits are within 4 of 0x8000 (a bf16
+// rounding midpoint).  Valid for finite, non-zero scales.
+static int8_t quant_packed_bf16(float w, float s, float rcp, long* slow_count) {
+  volatile float x = w * rcp;
+  if (((f_to_bits(x) + 4u) & 0xFFF8u) == 0x8000u) {
+    ++*slow_count;
+    return quant_exact<BF16>(w, s);
+  }
+  float y = round_bf16(x);
+  if (y > 127.0f) y = 127.0f;
+  if (y < -127.0f) y = -127.0f;
+  volatile float z = y + 12582912.0f;
+  return static_cast<int8_t>(f_to_bits(z) & 0xFF);
+}
+
+static void run_packed_bf16(int stride) {
+  std::vector<float> scales, weights;
+  for (uint32_t h = 1; h < 0x7F80u; ++h) scales.push_back(bf16_to_f(static_cast<uint16_t>(h)));
+  for (uint32_t h = 0; h < 0x10000u; ++h) {
+    const float v = bf16_to_f(static_cast<uint16_t>(h));
+    if (std::isfinite(v)) weights.push_back(v);
+  }
+  const int nt = std::max(1u, std::thread::hardware_concurrency());
+  std::vector<long> mism(nt, 0), slow(nt, 0), total(nt, 0);
+  std::vector<std::thread> th;
+  for (int t = 0; t < nt; ++t) {
+    th.emplace_back([&, t] {
+      for (size_t i = static_cast<size_t>(t) * stride; i < scales.size(); i += static_cast<size_t>(nt) * stride) {
+        const float s = scales[i];
+        volatile float one = 1.0f;
+        const float rcp = one / s;
+        if (!(rcp < 1.0e30f)) continue;  // the kernel takes the exact path for such scales
+        for (float w : weights) {
+          if (quant_packed_bf16(w, s, rcp, &slow[t]) != quant_exact<BF16>(w, s)) ++mism[t];
+          ++total[t];
+        }
+      }
+    });
+  }
+  for (auto& x : th) x.join();
+  long m = 0, sl = 0, tot = 0;
+  for (int t = 0; t < nt; ++t) { m += mism[t]; sl += slow[t]; tot += total[t]; }
+  std::printf("mismatches=%ld slow=%ld total=%ld\n", m, sl, tot);
+}
+
 static void run_packed(int stride) {
   std::vector<float> scales, weights;
   for (uint32_t h = 1; h < 0x7C00u; ++h) scales.push_back(f16_to_f(static_cast<uint16_t>(h)));
@@ -226,6 +274,7 @@ int main(int argc, char** argv) {
   else if (!std::strcmp(argv[1], "f32")) run<F32>(stride);
   else if (!std::strcmp(argv[1], "f16packed")) run_packed(stride);
   else if (!std::strcmp(argv[1], "f16packed_noclamp")) run_packed_noclamp(stride);
+  else if (!std::strcmp(argv[1], "bf16packed")) run_packed_bf16(stride);
   else return 2;
   return 0;
 }

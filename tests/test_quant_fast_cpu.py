@@ -7,7 +7,8 @@ sweep, and the packed fp16 path (quant4_f16: fp16 clamp and +1536
 round-to-integer) the same way.  The clamp-free packed path is swept over every
 (w, s) a row can hold when its scale is a normal fp16 number (|w| <= the row
 maximum that gives s; 9.3e8 pairs at stride 1).  The full sweep (every scale: 2.0e9 fp16 and 2.1e9 bf16
-pairs, and the clamp-free sweep) was run once with stride 1 and also found no mismatch.
+pairs, the clamp-free sweep and the packed bf16 sweep over 1.9e9 pairs) was run once with stride 1 and also
+found no mismatch.
 """
 import shutil
 import subprocess
@@ -30,7 +31,7 @@ def checker(tmp_path_factory):
 
 
 @pytest.mark.parametrize("dtype,stride", [("f16", 16), ("bf16", 16), ("f32", 1), ("f16packed", 16),
-                                          ("f16packed_noclamp", 4)])
+                                          ("f16packed_noclamp", 4), ("bf16packed", 16)])
 def test_fast_quantiser_matches_exact_division(checker, dtype, stride):
     out = subprocess.run([str(checker), dtype, str(stride)], capture_output=True, text=True, check=True).stdout
     fields = dict(kv.split("=") for kv in out.split())
