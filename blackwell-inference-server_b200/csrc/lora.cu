@@ -223,7 +223,10 @@ constexpr int kReqGroups = 4;                      // epilogue groups of 4 warps
 constexpr int kReqSlots = 2 * kReqGroups;          // TMEM accumulator slots, 64 columns each
 constexpr int kReqTmemCols = kReqSlots * 64 <= 256 ? 256 : 512;  // allocation: a power of two
 static_assert(kReqSlots * 64 <= 512, "TMEM holds 512 columns");
-constexpr int kReqThreads = 64 + 128 * kReqGroups; // warp 0 TMA, warp 1 MMA/TMEM, then the epilogue
+// warp 0 TMA, warp 1 MMA/TMEM, then the epilogue groups, then a second MMA warp.  Each tcgen05.mma
+// keeps its issuing thread ~120 cycles whatever N, so two issuers (alternate items) double the MMA rate.
+constexpr int kReqMmaWarp2 = 2 + 4 * kReqGroups;
+constexpr int kReqThreads = 64 + 128 * kReqGroups + 32;
 constexpr int kReqEpiThreads = 128 * kReqGroups;
 constexpr int kReqMaxStages = 12;
 constexpr int kReqSmemLimit = 232448;              // 227 KB of dynamic shared memory per CTA
@@ -348,8 +351,8 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   uint64_t* dempty = dfull + kReqSlots;  // kReqSlots
   uint64_t* full = dempty + kReqSlots;   // S
   uint64_t* empty = full + S;            // S
-  uint64_t* final_bar = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  uint64_t* final_bar = empty + S;       // 2, one per MMA issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_gen = abort_flag + 1;  // barrier generation seen at entry
   ReqProblem* sp = reinterpret_cast<ReqProblem*>(smem + batch.off_bar + 512);  // problem table
@@ -365,7 +368,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bfull[b], 1);
-      mbar_init(&bempty[b], 1);
+      mbar_init(&bempty[b], 2);  // both MMA issuers release a B buffer
     }
     for (int d = 0; d < kReqSlots; ++d) {
       mbar_init(&dfull[d], 1);
@@ -375,7 +378,8 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1 + 4);  // MMA commit + the 4 warps of the item's group
     }
-    mbar_init(final_bar, 1);
+    mbar_init(&final_bar[0], 1);
+    mbar_init(&final_bar[1], 1);
     *abort_flag = 0;
     *s_gen = ld_acquire_gpu(&gsync[1]);  // before this CTA arrives: the same value in every CTA
     fence_mbar_init();
@@ -434,9 +438,12 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         req_walk_next(w, sp, count);
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 || warp == kReqMmaWarp2) {
+    // ---------------- MMA issuers: items alternate between the two ----------------
+    // Both walk every item so that they take the same B-buffer steps; each item's MMAs
+    // come from one thread in one accumulator, so its sums are those of lora_merge.
     if (lane == 0) {
+      const int me = warp == 1 ? 0 : 1;
       const uint32_t idesc = make_idesc_f16(128, 64, false, true);
       const uint32_t sB_u32 = smem_u32(sB);
       const uint32_t ring_u32 = smem_u32(sRing) + 16384;  // A panel of stage 0
@@ -457,6 +464,10 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
           ++bseq;
           if (!mbar_wait(&bfull[bseq & 1], (bseq >> 1) & 1, abort_flag, kSiteReqB)) break;
         }
+        if ((it & 1) != me) {
+          req_walk_next(w, sp, count);
+          continue;
+        }
         const int st = it % S;
         const int d = it % kReqSlots;
         if (!mbar_wait(&full[st], (it / S) & 1, abort_flag, kSiteReqFull) ||
@@ -474,8 +485,8 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         umma_commit(&empty[st]);
         req_walk_next(w, sp, count);
       }
-      umma_commit(final_bar);  // every issued MMA has completed before TMEM is freed
-      mbar_wait(final_bar, 0, nullptr, kSiteReqFinal);
+      umma_commit(&final_bar[me]);  // every issued MMA has completed before TMEM is freed
+      mbar_wait(&final_bar[me], 0, nullptr, kSiteReqFinal);
     }
   } else {
     // ---------------- epilogue: warps 2 .. 2 + 4*kReqGroups - 1 ----------------
