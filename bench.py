@@ -265,8 +265,7 @@ class GemmSweepWorkload:
         self.dev = dev
         self.name = name
         self.m = m
-        # M <= 128 runs the persistent kernel, larger M the one-tile-per-CTA kernel
-        self.kernel = "w8a16_persistent_kernel" if m <= 128 else "w8a16_tc_kernel"
+        self.kernel = "w8a16_persistent_kernel"
         g = torch.Generator(device=dev).manual_seed(2000 + rank)
         if name == "cfg1":
             shapes = [(1024, 3072)] * 64

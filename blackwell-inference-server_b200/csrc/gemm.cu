@@ -4,24 +4,14 @@
 // (src/blackwell_ops/kernels/int8_gemm.py:15-60 kernel, :71-107 launcher):
 //     y[m, n] = dt( fp32( sum_k x[m,k] * w_int8[n,k] ) * fp32(scale[n]) ),  dt = x.dtype
 //
-// Formulation ("swap AB"): the CTA tile is 128 weight rows (the UMMA M
-// dimension) x BM tokens (the UMMA N dimension, 16..256), so a decode call with
-// M = 1..16 tokens still fills the 128-row tensor-core datapath and the op
-// streams the int8 weight from HBM exactly once.
-//
-// Per CTA, warp-specialised (192 threads):
-//   warp 0      TMA producer: int8 W tile [128 rows x 128 B] and activation
-//               tile [BM rows x 128 cols] (two 64-column panels), both
-//               128-byte swizzled, into a STAGES-deep ring.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//               (kind::f16, fp32 accumulator in TMEM, 128 x BM).
-//   warps 2-5   converters: int8 -> f16/bf16 (exact, integer-bias trick) into
-//               the K-major SW128 operand layout the tensor core reads
-//               (ASTAGES-deep ring); afterwards the epilogue: tcgen05.ld of the
-//               accumulator (thread = weight row), x scale[n], round, store.
-// Split-K (small M, few N tiles): each split writes fp32 partials to the
-// workspace; the last CTA of a tile (atomic ticket) sums the splits in split
-// order (deterministic) and resets the tile's counter to zero.
+// Formulation ("swap AB"): a work unit is 128 weight rows (the UMMA M
+// dimension) x BM tokens (the UMMA N dimension, 16..128) x a K range, so a
+// decode call with M = 1..16 tokens still fills the 128-row tensor-core
+// datapath and the op streams the int8 weight from HBM exactly once.  One
+// persistent kernel serves every M (details above its definition).  Split-K
+// (few tiles for the SMs) writes fp32 partials to the workspace; the last CTA
+// of a tile (atomic ticket) sums the splits in split order (deterministic) and
+// resets the tile's counter to zero.
 //
 // Layouts that TMA cannot address (unaligned base, row strides that are not
 // multiples of 16 bytes) go to a CUDA-core kernel with the same arithmetic.
@@ -32,38 +22,6 @@
 #include "common.cuh"
 
 namespace bw {
-
-enum GemmWaitSite : int {
-  kSiteProdEmpty = 101,
-  kSiteConvFull = 102,
-  kSiteConvAEmpty = 103,
-  kSiteMmaAFull = 104,
-  kSiteMmaFull = 105,
-  kSiteEpiTmem = 106,
-  kSiteDrain = 107,
-};
-
-template <int BM>
-struct GemmCfg {
-  static constexpr int BN = 128;  // weight rows per CTA (UMMA M)
-  static constexpr int BK = 128;  // K per stage
-  static constexpr int STAGES = BM >= 256 ? 2 : (BM >= 128 ? 3 : 4);
-  static constexpr int ASTAGES = 2;
-  static constexpr int W_BYTES = BN * BK;       // int8 tile
-  static constexpr int X_PANEL = BM * 128;      // one 64-column panel of x (16-bit)
-  static constexpr int X_BYTES = 2 * X_PANEL;   // 128 columns
-  static constexpr int A_PANEL = BN * 128;      // one 64-column panel of dequantised W
-  static constexpr int A_BYTES = 2 * A_PANEL;
-  static constexpr int TMEM_COLS = BM < 32 ? 32 : BM;
-  static constexpr int OFF_W = 0;
-  static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
-  static constexpr int OFF_A = OFF_X + STAGES * X_BYTES;
-  static constexpr int OFF_BAR = OFF_A + ASTAGES * A_BYTES;
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
-  static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert((2 * STAGES + 2 * ASTAGES + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
-};
 
 template <bool BF16>
 __device__ __forceinline__ void convert_chunk(const uint4& v, uint4& o0, uint4& o1) {
@@ -86,226 +44,14 @@ __device__ __forceinline__ void store_out(void* y, int64_t idx, float v) {
   else static_cast<__half*>(y)[idx] = __float2half_rn(v);
 }
 
-template <int BM, bool BF16>
-__global__ void __launch_bounds__(192, 1)
-    w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                    const void* __restrict__ scale, int sdtype, void* __restrict__ y, int64_t ldy, int M, int N,
-                    int kblocks, int kb_per_split, int splits, float* __restrict__ ws, int* __restrict__ counters) {
-  using C = GemmCfg<BM>;
-  constexpr int STAGES = C::STAGES;
-  constexpr int ASTAGES = C::ASTAGES;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sW = smem + C::OFF_W;
-  uint8_t* sX = smem + C::OFF_X;
-  uint8_t* sA = smem + C::OFF_A;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* empty = full + STAGES;
-  uint64_t* afull = empty + STAGES;
-  uint64_t* aempty = afull + ASTAGES;
-  uint64_t* tfull = aempty + ASTAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* ticket = abort_flag + 1;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  // M-tile fastest: the CTAs that share a weight tile are launched side by side and read it once
-  const int m_tile = blockIdx.x;
-  const int n_tile = blockIdx.y;
-  const int split = blockIdx.z;
-  const int n0 = n_tile * 128;
-  const int m0 = m_tile * BM;
-  const int kb0 = split * kb_per_split;
-  const int nkb = min(kb_per_split, kblocks - kb0);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4 + 1);  // 4 converter warps + 1 MMA commit
-    }
-    for (int t = 0; t < ASTAGES; ++t) {
-      mbar_init(&afull[t], 4);
-      mbar_init(&aempty[t], 1);
-    }
-    mbar_init(tfull, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_w);
-    tma_prefetch_desc(&tm_x);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // a weight tile read by several M-tiles stays in L2 for its neighbours; read once, it streams
-      const uint64_t pol_w = gridDim.x > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
-      const uint64_t pol_x = l2_policy_evict_last();
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, kSiteProdEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], C::W_BYTES + C::X_BYTES);
-        const int kx = (kb0 + i) * C::BK;
-        tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], kx, n0, pol_w);
-        tma_load_2d(sX + s * C::X_BYTES, &tm_x, &full[s], kx, m0, pol_x);
-        tma_load_2d(sX + s * C::X_BYTES + C::X_PANEL, &tm_x, &full[s], kx + 64, m0, pol_x);
-        issued = i + 1;
-      }
-      if (*abort_flag) {
-        // drain: no TMA write may land in shared memory after this CTA exits
-        for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
-          mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, kSiteDrain);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(128, BM, BF16, false);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
-        const int t = i % ASTAGES;
-        const uint32_t pa = (i / ASTAGES) & 1;
-        if (!mbar_wait(&afull[t], pa, abort_flag, kSiteMmaAFull)) break;
-        if (!mbar_wait(&full[s], ph, abort_flag, kSiteMmaFull)) break;
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + t * C::A_BYTES);
-        const uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t p = kk >> 2, q = kk & 3;
-          const uint64_t ad = make_sdesc(a_base + p * C::A_PANEL + q * 32, 16, 1024, kLayoutSW128);
-          const uint64_t bd = make_sdesc(x_base + p * C::X_PANEL + q * 32, 16, 1024, kLayoutSW128);
-          umma_f16(tmem, ad, bd, idesc, (i | kk) != 0 ? 1u : 0u);
-        }
-        umma_commit(&empty[s]);
-        umma_commit(&aempty[t]);
-      }
-      umma_commit(tfull);  // always: the epilogue and teardown wait on it
-    }
-  } else {
-    // ---------------- converters ----------------
-    const int crow = (warp - 2) * 32 + lane;  // tile row this thread converts
-    const int sw = crow & 7;
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % STAGES;
-      const uint32_t ph = (i / STAGES) & 1;
-      const int t = i % ASTAGES;
-      const uint32_t pa = (i / ASTAGES) & 1;
-      if (!mbar_wait(&full[s], ph, abort_flag, kSiteConvFull)) break;
-      if (!mbar_wait(&aempty[t], pa ^ 1, abort_flag, kSiteConvAEmpty)) break;
-      const uint8_t* src = sW + s * C::W_BYTES + crow * 128;
-      uint8_t* dst = sA + t * C::A_BYTES + crow * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
-        uint4 o0, o1;
-        convert_chunk<BF16>(v, o0, o1);
-        const int p = c >> 2;
-        const int j0 = (2 * c) & 7;
-        *reinterpret_cast<uint4*>(dst + p * C::A_PANEL + ((j0 ^ sw) << 4)) = o0;
-        *reinterpret_cast<uint4*>(dst + p * C::A_PANEL + (((j0 + 1) ^ sw) << 4)) = o1;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&afull[t]);
-        mbar_arrive(&empty[s]);
-      }
-    }
-    // ---------------- epilogue ----------------
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;
-    const int n = n0 + row;
-    const bool ok = mbar_wait(tfull, 0, abort_flag, kSiteEpiTmem);
-    tc_fence_after();
-    const bool bad = named_bar_any(1, 128, !ok || *abort_flag);  // same decision in all 4 warps
-    if (!bad) {
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-      if (splits == 1) {
-        const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
-#pragma unroll
-        for (int c0 = 0; c0 < BM; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c0, r);
-          tmem_ld_wait();
-          if (n < N) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = m0 + c0 + j;
-              if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, __uint_as_float(r[j]) * sc);
-            }
-          }
-        }
-      } else {
-        const int tile = m_tile * gridDim.y + n_tile;
-        float* mine = ws + (static_cast<size_t>(tile) * splits + split) * (128 * BM) + static_cast<size_t>(row) * BM;
-#pragma unroll
-        for (int c0 = 0; c0 < BM; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c0, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            *reinterpret_cast<float4*>(mine + c0 + j) = make_float4(
-                __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-        }
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (warp == 2 && lane == 0) *ticket = atomicAdd(&counters[tile], 1);
-        named_bar_sync(1, 128);
-        if (*ticket == splits - 1) {
-          __threadfence();
-          const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
-          const float* base = ws + static_cast<size_t>(tile) * splits * (128 * BM) + static_cast<size_t>(row) * BM;
-          for (int c0 = 0; c0 < BM; c0 += 4) {
-            float4 acc = __ldcg(reinterpret_cast<const float4*>(base + c0));
-            for (int sp = 1; sp < splits; ++sp) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(base + static_cast<size_t>(sp) * 128 * BM + c0));
-              acc.x += v.x;
-              acc.y += v.y;
-              acc.z += v.z;
-              acc.w += v.w;
-            }
-            if (n < N) {
-              const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const int m = m0 + c0 + j;
-                if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, a4[j] * sc);
-              }
-            }
-          }
-          if (warp == 2 && lane == 0) counters[tile] = 0;
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
-  }
-}
-
 // ---------------------------------------------------------------------------
-// Persistent variant for M <= 128 (decode and short prefill).
+// Persistent W8A16 GEMM for every M (decode, prefill).
 //
-// One CTA per SM walks work units (n_tile, m_tile, k-split) with a stride of
-// gridDim.x; the TMA producer streams W/x stages continuously across units, so
-// the weight stream never drains between tiles.  448 threads:
+// One CTA per SM walks work units (m_tile fastest, then n_tile, then k-split)
+// with a stride of gridDim.x; the TMA producer streams W/x stages continuously
+// across units, so the weight stream never drains between tiles, and the units
+// that share a weight tile run side by side (one DRAM read, the rest from L2).
+// 448 threads:
 //   warp 0       TMA producer (STAGES-deep ring of [W int8 128x128 B | x BM x 128])
 //   warp 1       TMEM owner (512 columns) + tcgen05.mma issuer
 //   warps 2-9    dequantisers in two groups of four that take alternate k-blocks
@@ -417,15 +163,19 @@ __global__ void __launch_bounds__(448, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
+      // a weight tile used by several M-tiles stays in L2 for the neighbours that share it
+      const int m_tiles = units / (n_tiles * splits);
+      const uint64_t pol_w = m_tiles > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       // (unit, k-block) walk of this CTA
       int u = blockIdx.x, i = 0;
       auto unit_kb = [&](int uu, int& nt, int& mt, int& kb0, int& nkb) {
         const int sp = uu % splits;
         const int t = uu / splits;
-        nt = t % n_tiles;
-        mt = t / n_tiles;
+        // M-tile fastest: the units that share a weight tile are consecutive
+        const int m_tiles_u = units / (n_tiles * splits);
+        mt = t % m_tiles_u;
+        nt = t / m_tiles_u;
         kb0 = sp * kb_per_split;
         nkb = min(kb_per_split, kblocks - kb0);
       };
@@ -587,8 +337,9 @@ __global__ void __launch_bounds__(448, 1)
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
       const int sp = u % splits;
       const int t = u / splits;
-      const int nt = t % n_tiles;
-      const int mt = t / n_tiles;
+      const int m_tiles_u = units / (n_tiles * splits);
+      const int mt = t % m_tiles_u;
+      const int nt = t / m_tiles_u;
       const int n = nt * 128 + row;
       const int m0 = mt * BM;
       const int b = j & 1;
@@ -708,7 +459,6 @@ __global__ void __launch_bounds__(128) w8a16_simt_kernel(const void* __restrict_
 // host planning
 // ---------------------------------------------------------------------------
 struct GemmPlan {
-  bool persistent = false;  // w8a16_persistent_kernel (M <= 128) or w8a16_tc_kernel
   int bm = 16;
   int n_tiles = 0, m_tiles = 0, kblocks = 0, splits = 1, kb_per_split = 0, units = 0, grid = 0;
   size_t counter_bytes = 0, partial_bytes = 0;
@@ -722,43 +472,32 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k) {
   const int sms = num_sms();
   p.n_tiles = static_cast<int>((n + 127) / 128);
   p.kblocks = static_cast<int>((k + 127) / 128);
-  if (m <= 128) {
-    p.persistent = true;
-    p.bm = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
-    p.m_tiles = 1;
-    const int tiles = p.n_tiles;
-    double best = 1e300;
-    for (int sp = 1; sp <= p.kblocks && sp <= 32; ++sp) {
-      const int kbps = (p.kblocks + sp - 1) / sp;
-      const int real = (p.kblocks + kbps - 1) / kbps;
-      if (real != sp) continue;
-      const long units = static_cast<long>(tiles) * sp;
-      const long per_cta = (units + sms - 1) / sms;
-      const double unit_cost = kbps * 16384.0 + 6000.0 + (sp > 1 ? 2.0 * 128 * p.bm * 4 : 0.0);
-      const double cost = per_cta * unit_cost;
-      if (cost < best * 0.97) {
-        best = cost;
-        p.splits = sp;
-        p.kb_per_split = kbps;
-      }
+  p.bm = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
+  p.m_tiles = static_cast<int>((m + p.bm - 1) / p.bm);
+  const int64_t tiles = static_cast<int64_t>(p.n_tiles) * p.m_tiles;
+  // split-K count: cost model over the units each CTA walks (weight bytes per unit,
+  // a fixed per-unit cost, the partials a split writes)
+  double best = 1e300;
+  for (int sp = 1; sp <= p.kblocks && sp <= 32; ++sp) {
+    const int kbps = (p.kblocks + sp - 1) / sp;
+    const int real = (p.kblocks + kbps - 1) / kbps;
+    if (real != sp) continue;
+    const int64_t units = tiles * sp;
+    const int64_t per_cta = (units + sms - 1) / sms;
+    const double unit_cost = kbps * 16384.0 + 6000.0 + (sp > 1 ? 2.0 * 128 * p.bm * 4 : 0.0);
+    const double cost = static_cast<double>(per_cta) * unit_cost;
+    if (cost < best * 0.97) {
+      best = cost;
+      p.splits = sp;
+      p.kb_per_split = kbps;
     }
-    p.units = tiles * p.splits;
-    p.grid = p.units < sms ? p.units : sms;
-  } else {
-    p.bm = 128;
-    p.m_tiles = static_cast<int>((m + p.bm - 1) / p.bm);
-    const int tiles = p.n_tiles * p.m_tiles;
-    int splits = tiles < sms ? sms / tiles : 1;
-    if (splits > p.kblocks) splits = p.kblocks;
-    if (splits < 1) splits = 1;
-    p.kb_per_split = (p.kblocks + splits - 1) / splits;
-    p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
-    p.units = tiles * p.splits;
   }
+  const int64_t units = tiles * p.splits;
+  p.units = units > INT32_MAX ? -1 : static_cast<int>(units);  // -1: too many units (refused by the caller)
+  p.grid = units < sms ? static_cast<int>(units) : sms;
   if (p.splits > 1) {
-    const size_t tiles = static_cast<size_t>(p.n_tiles) * p.m_tiles;
-    p.counter_bytes = ((tiles * sizeof(int) + 255) / 256) * 256;
-    p.partial_bytes = tiles * p.splits * 128 * p.bm * sizeof(float);
+    p.counter_bytes = ((static_cast<size_t>(tiles) * sizeof(int) + 255) / 256) * 256;
+    p.partial_bytes = static_cast<size_t>(tiles) * p.splits * 128 * p.bm * sizeof(float);
   }
   return p;
 }
@@ -793,36 +532,15 @@ static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUt
                     "cudaLaunchKernelEx(w8a16_persistent_kernel)");
 }
 
-template <int BM, bool BF16>
-static int launch_tc(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale, int sdt,
-                     void* y, int64_t ldy, int M, int N, float* ws, int* counters, cudaStream_t st) {
-  using C = GemmCfg<BM>;
-  static std::once_flag once[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(w8a16_tc_kernel<BM, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  });
-  if (int s = check_cuda(attr_err, "cudaFuncSetAttribute(w8a16_tc_kernel)")) return s;
-  dim3 grid(p.m_tiles, p.n_tiles, p.splits);
-  w8a16_tc_kernel<BM, BF16><<<grid, 192, C::SMEM, st>>>(tw, tx, scale, sdt, y, ldy, M, N, p.kblocks,
-                                                          p.kb_per_split, p.splits, ws, counters);
-  return check_launch("w8a16_tc_kernel");
-}
-
 template <bool BF16>
-static int dispatch_tc(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale, int sdt,
-                       void* y, int64_t ldy, int M, int N, float* ws, int* counters, cudaStream_t st) {
-  if (p.persistent) {
-    switch (p.bm) {
-      case 16: return launch_persistent<16, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-      case 32: return launch_persistent<32, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-      case 64: return launch_persistent<64, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-      default: return launch_persistent<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-    }
+static int dispatch_gemm(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale, int sdt,
+                         void* y, int64_t ldy, int M, int N, float* ws, int* counters, cudaStream_t st) {
+  switch (p.bm) {
+    case 16: return launch_persistent<16, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+    case 32: return launch_persistent<32, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+    case 64: return launch_persistent<64, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+    default: return launch_persistent<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
   }
-  return launch_tc<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
 }
 
 static bool tma_ok(const void* p, int64_t ld_bytes) {
@@ -872,6 +590,8 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   }
 
   const GemmPlan p = plan_gemm(m, n, k);
+  if (p.units < 0) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: m=%lld n=%lld is too many output tiles",
+                               (long long)m, (long long)n);
   float* ws = nullptr;
   int* counters = nullptr;
   if (p.splits > 1) {
@@ -890,8 +610,8 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   if (int s = make_tmap_2d(&tx, x, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m, k,
                            ldx * 2, p.bm, 64, CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
-  if (bf16) return dispatch_tc<true>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
-  return dispatch_tc<false>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
+  if (bf16) return dispatch_gemm<true>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
+  return dispatch_gemm<false>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
 }
 
 // ---------------------------------------------------------------------------
