@@ -440,7 +440,7 @@ class NSplitWorkload:
     kernel = "w8a16_persistent_kernel"
     name = "cfg5"
 
-    def __init__(self, dev, rank, world, m, adapters=32, group=None):
+    def __init__(self, dev, rank, world, m, adapters=32, group=None, gather="fused"):
         from blackwell_ops import _lib
         from blackwell_ops.cuda import lora_merge_requant_batched
         from blackwell_ops.nsplit import shard_rows
@@ -480,6 +480,19 @@ class NSplitWorkload:
         self.ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
         self.variants = len(self.ranks_r)
         self.launches_per_step = len(self.shapes)
+        self.gather = gather if world > 1 else "none"
+        self.fused_layers = None
+        if self.gather == "fused":
+            from blackwell_ops.nsplit import ColumnParallelW8A16
+
+            # one layer per projection; the adapter of a step swaps its weight shard in
+            self.fused_layers = [ColumnParallelW8A16(self.Q[0][j], self.S[0][j], n, group=group, fused=True)
+                                 for j, (_, n) in enumerate(self.shapes)]
+            for j, layer in enumerate(self.fused_layers):
+                if not layer.fused:
+                    raise SystemExit("cfg5 fused gather needs at least one output column per rank")
+                layer.fused_forward(self.X[j], out=self.Y[j])  # sets up the symmetric buffers (collective)
+            torch.cuda.synchronize()
         self.metric_kind = "gbs" if m < 512 else "tflops"
         self.unit = "GB/s" if m < 512 else "TFLOPS"
         # whole-job algorithmic work of one step (all ranks together)
@@ -490,10 +503,15 @@ class NSplitWorkload:
         self.flops = sum(2.0 * m * per * k for (k, _), per in zip(self.shapes, self.per))
 
     def config(self):
-        return workload_config("cfg5", self.m) | {"gpus": self.world}
+        return workload_config("cfg5", self.m) | {"gpus": self.world, "gather": self.gather}
 
     def step(self, s, st, events=None):
         ai = s % len(self.ranks_r)
+        if self.fused_layers is not None:
+            for j, layer in enumerate(self.fused_layers):
+                layer.w, layer.scale = self.Q[ai][j], self.S[ai][j]
+                layer.fused_forward(self.X[j], out=self.Y[j])
+            return
         for j, ((k, n), per) in enumerate(zip(self.shapes, self.per)):
             rc = self.lib.bw_w8a16_gemm(self.X[j].data_ptr(), 1, k, self.Q[ai][j].data_ptr(), k,
                                         self.S[ai][j].data_ptr(), 0, self.Yloc[j].data_ptr(), per, self.m, per, k,
@@ -519,7 +537,11 @@ class NSplitWorkload:
         ai = s % len(self.ranks_r)
         for j, (k, n) in enumerate(self.shapes):
             x = self.hX[j].to(self.dev, non_blocking=True)
-            layer = ColumnParallelW8A16(self.Q[ai][j], self.S[ai][j], n, group=self.group)
+            if self.fused_layers is not None:
+                layer = self.fused_layers[j]
+                layer.w, layer.scale = self.Q[ai][j], self.S[ai][j]
+            else:
+                layer = ColumnParallelW8A16(self.Q[ai][j], self.S[ai][j], n, group=self.group)
             self.hY[j].copy_(layer(x), non_blocking=True)
 
     def cpu_sample(self, step_index: int):
@@ -550,7 +572,8 @@ def make_workload(args, dev, rank, world):
     if args.workload == "quant":
         return QuantizeWorkload(dev, rank, world)
     if args.workload == "cfg5":
-        return NSplitWorkload(dev, rank, world, args.m if args.m else 16, adapters=args.adapters)
+        return NSplitWorkload(dev, rank, world, args.m if args.m else 16, adapters=args.adapters,
+                              gather=args.gather)
     raise SystemExit(f"unknown workload {args.workload}")
 
 
@@ -643,7 +666,8 @@ def workload_config(name: str, m: int) -> dict:
                     f"(r in {{16,64,128}}), M={m}, bf16"}[name]
     if name == "cfg5":
         return {"workload": desc, "m": m, "l2": "inputs larger than L2 (470 MB of int8 weights per adapter step)",
-                "parallelism": "column-parallel N-split over the GPUs, NCCL all-gather of output slices (strong)"}
+                "parallelism": "column-parallel N-split over the GPUs, output slices all-gathered inside the GEMM "
+                               "epilogue over peer memory (--gather fused) or by NCCL (--gather nccl); strong"}
     return {"workload": desc, "m": m, "l2": "inputs larger than L2 (weights streamed from HBM each step)",
             "parallelism": "weak: independent replicas per rank"}
 
@@ -661,6 +685,8 @@ def main():
     ap.add_argument("--workload", default="cfg2")
     ap.add_argument("--m", type=int, default=0, help="tokens for the GEMM workloads")
     ap.add_argument("--adapters", type=int, default=32, help="cfg5: number of adapters")
+    ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
+                    help="cfg5 on several GPUs: all-gather inside the GEMM epilogue over peer memory, or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

@@ -49,6 +49,9 @@ SIGNATURES = {
     "bw_w8a16_gemm_static_scratch_bytes": (_c.c_size_t, []),
     "bw_w8a16_gemm_noalloc": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
                                          _P]),
+    "bw_w8a16_gemm_allgather": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _c.POINTER(_c.c_void_p),
+                                           _I64, _I64, _I64, _I64, _I64, _c.POINTER(_c.c_void_p), _c.c_int,
+                                           _c.c_int, _P, _c.c_size_t, _P]),
     "bw_lora_delta": (_c.c_int, [_P, _P, _P, _I64, _I64, _I64, _c.c_float, _P]),
     "bw_add_delta": (_c.c_int, [_P, _P, _I64, _P]),
     "bw_lora_merge": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),

@@ -16,9 +16,17 @@ the rank's int8 copy.
 The local GEMM is a parameter so the sharding / gather logic can be exercised
 on CPU ranks (gloo) with any function of the same signature; the default is
 the tcgen05 kernel.
+
+``fused=True`` replaces GEMM + NCCL all-gather by one kernel per rank
+(``bw_w8a16_gemm_allgather``): the epilogue stores every output tile into
+every rank's output buffer over peer memory (a symmetric-memory buffer, plain
+stores over NVLink) and the ranks exchange bounded completion flags.  It needs
+CUDA ranks on one node and at least one output column per rank; otherwise the
+NCCL path runs.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
@@ -56,7 +64,8 @@ class ColumnParallelW8A16:
 
     def __init__(self, w_shard: torch.Tensor, scale_shard: torch.Tensor, n_total: int,
                  group: dist.ProcessGroup | None = None,
-                 local_gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor] | None = None):
+                 local_gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor] | None = None,
+                 fused: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -69,6 +78,10 @@ class ColumnParallelW8A16:
         self.per = per
         self.local_gemm = local_gemm or _default_gemm()
         self._use_into_tensor = True
+        # fused all-gather: every rank must own at least one real column (the same decision on all ranks)
+        self.fused = (fused and self.world > 1 and local_gemm is None and w_shard.is_cuda
+                      and (self.world - 1) * per < n_total)
+        self._symm: dict = {}
 
     def local(self, x: torch.Tensor) -> torch.Tensor:
         return self.local_gemm(x, self.w, self.scale)
@@ -89,5 +102,56 @@ class ColumnParallelW8A16:
             dist.all_gather(list(buf.unbind(0)), y_local, group=self.group)
         return buf.permute(1, 0, 2).reshape(m, self.world * self.per)[:, : self.n_total]
 
+    def _fused_buffers(self, m: int, dtype: torch.dtype, device: torch.device):
+        """Symmetric output buffer [M, G*Ns] and signal pads for this M (a collective on first use)."""
+        key = (m, dtype)
+        st = self._symm.get(key)
+        if st is None:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            group = self.group if self.group is not None else dist.group.WORLD
+            enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
+            if enable is not None:
+                enable(group.group_name)
+            y = symm_mem.empty((m, self.world * self.per), dtype=dtype, device=device)
+            hy = symm_mem.rendezvous(y, group.group_name)
+            sig = symm_mem.empty((64,), dtype=torch.int32, device=device)
+            sig.zero_()
+            hs = symm_mem.rendezvous(sig, group.group_name)
+            torch.cuda.synchronize(device)
+            dist.barrier(group=group)  # every rank's flags are zero before anyone signals
+            yp = (ctypes.c_void_p * self.world)(*[int(p) for p in hy.buffer_ptrs])
+            sp = (ctypes.c_void_p * self.world)(*[int(p) for p in hs.buffer_ptrs])
+            st = self._symm[key] = (y, hy, sig, hs, yp, sp)
+        return st
+
+    def fused_forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """One kernel per rank: local GEMM with the all-gather over peer memory in its epilogue."""
+        from ._lib import DTYPE_CODE, check, lib, stream_ptr
+        from .kernels.int8_gemm import _workspace
+
+        if x.dim() != 2 or x.dtype not in (torch.float16, torch.bfloat16):
+            raise RuntimeError("fused N-split: x must be a 2-D fp16 or bf16 tensor")
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        m, k = x.shape
+        n_valid = min(self.per, self.n_total - self.rank * self.per)
+        y, _, _, _, yp, sp = self._fused_buffers(m, x.dtype, x.device)
+        st = stream_ptr(x.device)
+        need = lib.bw_w8a16_gemm_workspace_size(m, n_valid, k)
+        ws = _workspace(x.device, st, need)
+        with torch.cuda.device(x.device):
+            check(lib.bw_w8a16_gemm_allgather(
+                x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0), self.w.data_ptr(), self.w.stride(0),
+                self.scale.data_ptr(), DTYPE_CODE[self.scale.dtype], yp, self.world * self.per, self.rank * self.per,
+                m, n_valid, k, sp, self.world, self.rank, ws.data_ptr() if ws is not None else None,
+                ws.numel() if ws is not None else 0, st), "int8_gemm (all-gather)")
+        if out is not None:
+            out.copy_(y[:, : self.n_total])
+            return out
+        return y[:, : self.n_total].clone()
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fused:
+            return self.fused_forward(x)
         return self.gather(self.local(x))

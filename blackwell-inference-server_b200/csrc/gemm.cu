@@ -44,6 +44,50 @@ __device__ __forceinline__ void store_out(void* y, int64_t idx, float v) {
   else static_cast<__half*>(y)[idx] = __float2half_rn(v);
 }
 
+// Column-parallel N-split with the all-gather fused into the epilogue: every
+// output element is stored into every rank's Y (peer memory over NVLink, plain
+// stores), guarded by two flag handshakes on the ranks' signal pads.
+struct GatherArgs {
+  unsigned long long y[8];    // each rank's Y [M, ldy]; this rank's columns start at col0
+  unsigned long long sig[8];  // each rank's signal pad (u32): [0,G) ready, [G,2G) done, [2G] CTA ticket,
+                              // [2G+1] epoch of the last completed call (all zero before the first call)
+  long long col0;
+  int world, rank;            // world == 0: a plain GEMM into y
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until every word of flags[0, n) equals v; false (and the site recorded) on timeout.
+__device__ __forceinline__ bool wait_flags(const uint32_t* flags, int n, uint32_t v, int site) {
+  const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
+  const long long t0 = clock64();
+  for (int p = 0; p < n; ++p) {
+    while (ld_acquire_sys(flags + p) != v) {
+      if (clock64() - t0 > limit) {
+        record_timeout(site);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+template <bool BF16>
+__device__ __forceinline__ void store_y(void* y, const GatherArgs& g, int64_t ldy, int m, int n, float v) {
+  if (g.world == 0) {
+    store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, v);
+  } else {
+    const int64_t idx = static_cast<int64_t>(m) * ldy + g.col0 + n;
+    for (int r = 0; r < g.world; ++r) store_out<BF16>(reinterpret_cast<void*>(g.y[r]), idx, v);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Persistent W8A16 GEMM for every M (decode, prefill).
 //
@@ -98,6 +142,8 @@ enum PersistentWaitSite : int {
   kSitePEpi = 117,
   kSitePDrain = 118,
   kSitePFinal = 119,
+  kSiteGReady = 130,
+  kSiteGDone = 131,
 };
 
 template <int BM, bool BF16>
@@ -105,7 +151,7 @@ __global__ void __launch_bounds__(448, 1)
     w8a16_persistent_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                             const void* __restrict__ scale, int sdtype, void* __restrict__ y, int64_t ldy, int M,
                             int N, int n_tiles, int kblocks, int kb_per_split, int splits, int units,
-                            float* __restrict__ ws, int* __restrict__ counters) {
+                            float* __restrict__ ws, int* __restrict__ counters, const GatherArgs g) {
   using C = PCfg<BM>;
   constexpr int STAGES = C::STAGES;
   constexpr int ASTAGES = C::ASTAGES;
@@ -333,6 +379,22 @@ __global__ void __launch_bounds__(448, 1)
     const int row = q * 32 + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::D_COL0;
     pdl_wait();
+    bool gather_ok = true;
+    uint32_t epoch = 0;
+    if (g.world > 0) {
+      // this call's epoch: one past the last completed call (kept on the device, so a captured
+      // graph replays correctly); ready handshake: this rank's Y may be overwritten now (its
+      // earlier readers are done), and no store goes to a peer before that peer has said the same
+      if (warp == 10 && lane == 0) {
+        const uint32_t* mine = reinterpret_cast<const uint32_t*>(g.sig[g.rank]);
+        epoch = ld_acquire_sys(mine + 2 * g.world + 1) + 1u;
+        if (blockIdx.x == 0)
+          for (int p = 0; p < g.world; ++p) st_release_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + g.rank, epoch);
+        gather_ok = wait_flags(mine, g.world, epoch, kSiteGReady);
+        if (!gather_ok) *abort_flag = 1;
+      }
+      gather_ok = !named_bar_any(1, 128, !gather_ok);
+    }
     int j = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
       const int sp = u % splits;
@@ -358,7 +420,7 @@ __global__ void __launch_bounds__(448, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int m = m0 + c0 + e;
-              if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, __uint_as_float(r[e]) * sc);
+              if (m < M) store_y<BF16>(y, g, ldy, m, n, __uint_as_float(r[e]) * sc);
             }
           }
         }
@@ -420,11 +482,29 @@ __global__ void __launch_bounds__(448, 1)
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int m = m0 + c0 + e;
-                if (m < M) store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, a[e] * sc);
+                if (m < M) store_y<BF16>(y, g, ldy, m, n, a[e] * sc);
               }
             }
           }
           if (warp == 10 && lane == 0) counters[t] = 0;
+        }
+      }
+    }
+    if (g.world > 0) {
+      // done handshake: the last CTA of this rank tells every peer that this rank's columns
+      // are in its Y, then waits until every peer has said the same (bounded)
+      named_bar_sync(1, 128);
+      if (warp == 10 && lane == 0) {
+        __threadfence_system();
+        uint32_t* mine = reinterpret_cast<uint32_t*>(g.sig[g.rank]);
+        if (atomicAdd(mine + 2 * g.world, 1u) == gridDim.x - 1) {
+          // every CTA of this call has read the epoch (it took a ticket after doing so)
+          __threadfence_system();
+          for (int p = 0; p < g.world; ++p)
+            st_release_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + g.world + g.rank, epoch);
+          wait_flags(mine + g.world, g.world, epoch, kSiteGDone);
+          atomicExch(mine + 2 * g.world, 0u);  // the CTA ticket, for the next call
+          st_release_sys(mine + 2 * g.world + 1, epoch);
         }
       }
     }
@@ -506,7 +586,8 @@ static bool g_use_pdl = true;
 
 template <int BM, bool BF16>
 static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale,
-                             int sdt, void* y, int64_t ldy, int M, int N, float* ws, int* counters, cudaStream_t st) {
+                             int sdt, void* y, int64_t ldy, int M, int N, float* ws, int* counters,
+                             const GatherArgs& g, cudaStream_t st) {
   using C = PCfg<BM>;
   static std::once_flag once[64];
   int dev = 0;
@@ -528,18 +609,19 @@ static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUt
   cfg.attrs = attr;
   cfg.numAttrs = g_use_pdl ? 1 : 0;
   return check_cuda(cudaLaunchKernelEx(&cfg, w8a16_persistent_kernel<BM, BF16>, tw, tx, scale, sdt, y, ldy, M, N,
-                                       p.n_tiles, p.kblocks, p.kb_per_split, p.splits, p.units, ws, counters),
+                                       p.n_tiles, p.kblocks, p.kb_per_split, p.splits, p.units, ws, counters, g),
                     "cudaLaunchKernelEx(w8a16_persistent_kernel)");
 }
 
 template <bool BF16>
 static int dispatch_gemm(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale, int sdt,
-                         void* y, int64_t ldy, int M, int N, float* ws, int* counters, cudaStream_t st) {
+                         void* y, int64_t ldy, int M, int N, float* ws, int* counters, const GatherArgs& g,
+                         cudaStream_t st) {
   switch (p.bm) {
-    case 16: return launch_persistent<16, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-    case 32: return launch_persistent<32, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-    case 64: return launch_persistent<64, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
-    default: return launch_persistent<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, st);
+    case 16: return launch_persistent<16, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
+    case 32: return launch_persistent<32, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
+    case 64: return launch_persistent<64, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
+    default: return launch_persistent<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
   }
 }
 
@@ -560,10 +642,10 @@ extern "C" size_t bw_w8a16_gemm_workspace_zeroed_bytes(int64_t m, int64_t n, int
   return bw::plan_gemm(m, n, k).counter_bytes;
 }
 
-extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
-                             const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n,
-                             int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
-  using namespace bw;
+namespace bw {
+static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
+                     int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace,
+                     size_t workspace_bytes, const GatherArgs& g, void* stream) {
   if (m < 0 || n < 0 || k < 1)
     return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: need m, n >= 0 and k >= 1 (got %lld, %lld, %lld)",
                 (long long)m, (long long)n, (long long)k);
@@ -581,6 +663,8 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   const bool bf16 = x_dtype == BW_DTYPE_BF16;
 
   if (!tma_ok(x, ldx * 2) || !tma_ok(w, ldw)) {
+    if (g.world > 0)
+      return fail(BW_ERR_UNSUPPORTED, "int8_gemm (all-gather): x and w must be 16-byte aligned with 16-byte row strides");
     dim3 grid(static_cast<unsigned>((n + 127) / 128), static_cast<unsigned>(m));
     if (bf16)
       w8a16_simt_kernel<true><<<grid, 128, 0, st>>>(x, ldx, w, ldw, scale, scale_dtype, y, ldy, (int)m, (int)n, (int)k);
@@ -610,8 +694,47 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   if (int s = make_tmap_2d(&tx, x, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m, k,
                            ldx * 2, p.bm, 64, CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
-  if (bf16) return dispatch_gemm<true>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
-  return dispatch_gemm<false>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, st);
+  if (bf16) return dispatch_gemm<true>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, g, st);
+  return dispatch_gemm<false>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, g, st);
+}
+}  // namespace bw
+
+extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                             const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n,
+                             int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
+  bw::GatherArgs g = {};
+  return bw::gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y, ldy, m, n, k, workspace, workspace_bytes, g,
+                       stream);
+}
+
+// Column-parallel N-split GEMM with the all-gather in the epilogue: this rank's output columns
+// [col0, col0 + n) are stored into every rank's Y over peer memory, then the ranks exchange
+// completion flags (bounded waits; a timeout shows in bw_device_status).
+extern "C" int bw_w8a16_gemm_allgather(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                                       const void* scale, int scale_dtype, void* const* y_ranks, int64_t ldy,
+                                       int64_t col0, int64_t m, int64_t n, int64_t k, void* const* signal_ranks,
+                                       int world, int rank, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace bw;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): need 1 <= world <= 8 and 0 <= rank < world");
+  if (!y_ranks || !signal_ranks) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): null pointer list");
+  if (col0 < 0 || col0 + n > ldy)
+    return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): columns [%lld, %lld) outside the row stride %lld",
+                (long long)col0, (long long)(col0 + n), (long long)ldy);
+  GatherArgs g = {};
+  for (int r = 0; r < world; ++r) {
+    if (!y_ranks[r] || !signal_ranks[r])
+      return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): null pointer for rank %d", r);
+    if (reinterpret_cast<uintptr_t>(signal_ranks[r]) % 4 != 0)
+      return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): signal pad of rank %d is not 4-byte aligned", r);
+    g.y[r] = reinterpret_cast<unsigned long long>(y_ranks[r]);
+    g.sig[r] = reinterpret_cast<unsigned long long>(signal_ranks[r]);
+  }
+  g.col0 = col0;
+  g.world = world;
+  g.rank = rank;
+  return gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y_ranks[rank], ldy, m, n, k, workspace,
+                   workspace_bytes, g, stream);
 }
 
 // ---------------------------------------------------------------------------

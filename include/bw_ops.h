@@ -95,6 +95,25 @@ int bw_w8a16_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, const int8_t*
                           int64_t n, int64_t k, void* stream);
 
 /*
+ * Column-parallel N-split W8A16 GEMM with the all-gather fused into the
+ * epilogue (the north star's N-split; the reference has no multi-GPU path).
+ * Rank `rank` of `world` (<= 8) holds w rows [0, n) of its shard and owns output
+ * columns [col0, col0 + n) of Y [m, ldy]; each output tile is stored straight
+ * into every rank's Y over peer memory (plain stores), so every rank ends with
+ * the whole Y.  y_ranks / signal_ranks are host arrays of `world` device
+ * pointers valid in this process (e.g. a symmetric-memory buffer's peer
+ * addresses); each signal pad holds >= 2*world + 2 u32 words, zero before the
+ * first call, and is not shared with other users.  Every rank must make the same
+ * calls in the same order, each with n >= 1; the ranks wait for one another
+ * inside the kernel with bounded waits (a timeout shows in bw_device_status).
+ * Workspace as bw_w8a16_gemm(m, n, k).  x and w must be TMA-addressable.
+ */
+int bw_w8a16_gemm_allgather(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                            const void* scale, int scale_dtype, void* const* y_ranks, int64_t ldy,
+                            int64_t col0, int64_t m, int64_t n, int64_t k, void* const* signal_ranks,
+                            int world, int rank, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * LoRA delta: delta[n, k] = fp16( fp32(sum_j b[n,j] * a[j,k]) * scaling ).
  * Replaces lora_delta (src/blackwell_ops/cuda/lora_ops.cu:43-60) and
  * lora_delta_tiled (src/blackwell_ops/cuda/lora_tiled.cu:88-103).

@@ -2,7 +2,8 @@
 
 Each rank quantises its row shard of the weight on its own GPU, runs the
 tcgen05 W8A16 GEMM on it, and the slices are all-gathered over NVLink into
-[M, N].  The result must equal the single-GPU GEMM of the full weight within
+[M, N], once with NCCL and once by the fused kernel that stores its tiles into
+every rank's output buffer over peer memory.  The result must equal the single-GPU GEMM of the full weight within
 the GEMM tolerance (max |err| <= 1e-2, relative <= 1e-3 against the fp32
 dequantise-matmul) and, row for row, the codes and scales of the full
 quantisation.  Needs two or more GPUs; skipped otherwise.
@@ -76,6 +77,26 @@ def _worker(rank, world, port, cases, out_dir):
             continue
         y = layer.gather(y_loc)
         torch.cuda.synchronize()
+        # the fused kernel (all-gather over peer memory in the GEMM epilogue): same result on every
+        # rank, on two calls in a row and from a replayed CUDA graph (the epoch lives on the device)
+        fused = ColumnParallelW8A16(q_loc, s_loc, n, fused=True)
+        outs = [fused(x), fused(x)]
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            yg = fused(x)
+        for _ in range(2):
+            gr.replay()
+        torch.cuda.synchronize()
+        outs.append(yg.clone())
+        del gr
+        try:
+            assert fused.fused == ((world - 1) * -(-n // world) < n), "fused path not taken"
+            for i, yf in enumerate(outs):
+                bound = 1e-2 + 2.0 ** (-10 if dt == "f16" else -7) * y.float().abs()
+                d = (yf.float() - y.float()).abs()
+                assert bool((d <= bound).all()), f"fused call {i}: |fused - nccl| up to {float(d.max())}"
+        except Exception as e:
+            failures.append(f"case {(m, n, k, dt)} fused: {type(e).__name__}: {e}")
         if rank == 0:
             try:
                 q_full, s_full = quantize_weight_int8(w)
@@ -108,7 +129,8 @@ def test_column_parallel_nccl_matches_single_gpu(tmp_path):
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 8)
-    cases = [(16, 3072, 1024, "f16"), (1, 1000, 512, "f16"), (64, 28672 // 8, 8192, "bf16"), (300, 4096, 1024, "bf16")]
+    cases = [(16, 3072, 1024, "f16"), (1, 1000, 512, "f16"), (64, 28672 // 8, 8192, "bf16"), (300, 4096, 1024, "bf16"),
+             (16, 1003, 2048, "bf16")]
     mp.spawn(_worker, args=(world, _free_port(), cases, str(tmp_path)), nprocs=world, join=True)
     for r in range(world):
         assert Path(tmp_path, f"rank{r}.txt").read_text() == "ok"
