@@ -9,9 +9,10 @@
 // decode call with M = 1..16 tokens still fills the 128-row tensor-core
 // datapath and the op streams the int8 weight from HBM exactly once.  One
 // persistent kernel serves every M (details above its definition).  Split-K
-// (few tiles for the SMs) writes fp32 partials to the workspace; the last CTA
-// of a tile (atomic ticket) sums the splits in split order (deterministic) and
-// resets the tile's counter to zero.
+// (few tiles for the SMs) or stream-K (many tiles: equal k-ranges per CTA)
+// writes fp32 pieces of split tiles to the workspace; the last CTA of a tile
+// (atomic ticket) sums them in k order (deterministic) and resets the tile's
+// counter to zero.
 //
 // Layouts that TMA cannot address (unaligned base, row strides that are not
 // multiples of 16 bytes) go to a CUDA-core kernel with the same arithmetic.
@@ -95,19 +96,33 @@ __device__ __forceinline__ void store_y(void* y, const GatherArgs& g, int64_t ld
 // with a stride of gridDim.x; the TMA producer streams W/x stages continuously
 // across units, so the weight stream never drains between tiles, and the units
 // that share a weight tile run side by side (one DRAM read, the rest from L2).
-// 448 threads:
-//   warp 0       TMA producer (STAGES-deep ring of [W int8 128x128 B | x BM x 128])
-//   warp 1       TMEM owner (512 columns) + tcgen05.mma issuer
+// 512 threads:
+//   warp 0       TMA producer of the weight tiles (STAGES-deep ring, 128 x 128 B)
+//   warp 15      TMA producer of the activation tiles (BM x 128 per stage)
+//   warp 1       TMEM owner (512 columns) + tcgen05.mma issuer 0
+//   warp 14      tcgen05.mma issuer 1 (BM <= 64)
 //   warps 2-9    dequantisers in two groups of four that take alternate k-blocks
 //                (thread = weight row, all 128 columns of the stage); int8 ->
 //                f16/bf16 straight into a TMEM A buffer (tcgen05.st), 4 x 64 cols
-//   warps 10-13  epilogue: double-buffered TMEM accumulators (2 x BM cols), so a
-//                unit's epilogue overlaps the next unit's mainloop
+//   warps 10-13  epilogue
 // The MMA is the TS form: A (dequantised W) from TMEM, B (x) from shared memory.
-// Programmatic dependent launch: the producer waits (griddepcontrol.wait) only
-// before its first x load and the epilogue before its first global access, so
-// a dependent launch can stream weights while its predecessor finishes.
+// A weight slot is released as soon as a dequantiser group has read it into
+// registers, before that group waits for a free TMEM buffer, and an x slot when
+// the MMAs that read it complete, so the weight ring stays full of loads in
+// flight.  With two issuers, issuer h issues the K=16 slices [4h, 4h+4) of every
+// k-block into its own accumulator and the epilogue adds the two (a fixed order,
+// so the result does not depend on timing).  Accumulators are double-buffered
+// (DBUF = 2), so a tile's epilogue overlaps the next tile's mainloop.
+// Programmatic dependent launch: the weight producer never waits for the
+// preceding kernel (weights do not depend on it); the activation producer and
+// the epilogue wait (griddepcontrol.wait) before their first global access.
 // ---------------------------------------------------------------------------
+#ifndef BW_GEMM_SMALL_ISSUERS
+#define BW_GEMM_SMALL_ISSUERS 2
+#endif
+#ifndef BW_GEMM_BM128_ISSUERS
+#define BW_GEMM_BM128_ISSUERS 1
+#endif
 template <int BM>
 struct PCfg {
   static constexpr int BK = 128;
@@ -120,16 +135,90 @@ struct PCfg {
   static constexpr int A_COL0 = 0;
   static constexpr int D_COL0 = ASTAGES * 64;
   static constexpr int TMEM_COLS = 512;
+  // MMA issuers and accumulator buffers per issuer: BM <= 64 fits 2 x 2 x BM columns;
+  // BM = 128 fits one issuer with two buffers (two issuers would leave one buffer each)
+  static constexpr int NI = BM <= 64 ? BW_GEMM_SMALL_ISSUERS : BW_GEMM_BM128_ISSUERS;
+  static constexpr int DBUF = NI == 2 && BM == 128 ? 1 : 2;
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = STAGES * W_BYTES;
   static constexpr int OFF_BAR = OFF_X + STAGES * X_BYTES;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
-  static constexpr int THREADS = 448;
+  static constexpr int THREADS = 512;
   static_assert(BM >= 16 && BM <= 128 && BM % 16 == 0, "UMMA N for M=128");
-  static_assert(D_COL0 + 2 * BM <= TMEM_COLS, "TMEM budget");
+  static_assert(NI == 1 || NI == 2, "one or two MMA issuers");
+  static_assert(D_COL0 + DBUF * NI * BM <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert((3 * STAGES + 2 * ASTAGES + 4 + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
+  static_assert((4 * STAGES + 2 * ASTAGES + 4 + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
+};
+
+// The workspace starts with a counter region of the same size for every shape,
+// so the fp32 pieces of one call never land where another shape keeps counters
+// (a workspace is shared by calls of different shapes): counters stay zero at
+// rest across any sequence of calls.
+constexpr int kGemmCounterSlots = 1024;
+constexpr size_t kGemmCounterBytes = kGemmCounterSlots * sizeof(int);
+
+// Work schedule of the persistent kernel.  A tile is 128 weight rows x BM tokens
+// (M-tile fastest: t = nt * m_tiles + mt) over `kblocks` k-blocks of 128.
+//   mode 0  split-K units: unit u = (tile u / splits, k-split u % splits), CTA b
+//           takes units b, b + grid, ...; a split tile's piece lives in slot
+//           [tile][split]
+//   mode 1  stream-K: the tiles' k-blocks laid end to end (tile-major) and cut
+//           into `grid` equal contiguous ranges, one per CTA, so every CTA
+//           streams the same number of weight bytes whatever the tile count; a
+//           tile cut by a range boundary is finished by the CTAs that share it,
+//           each writing its piece to slot [cta][0] (the CTA's first segment) or
+//           [cta][1] (its last)
+// Either way the last CTA to finish a split tile (atomic ticket) sums the
+// pieces in k order, so the result does not depend on timing.
+struct Sched {
+  int mode;
+  int n_tiles, m_tiles, kblocks;
+  int splits, kb_per_split, units;  // mode 0
+  long long work;                   // mode 1: tiles * kblocks
+};
+
+// One (tile, k-range) piece of a CTA's work.
+struct Seg {
+  int t, k0, nkb, split;  // split: k-split index (mode 0); 0 = first / 1 = later segment of the CTA (mode 1)
+};
+
+__device__ __forceinline__ long long sk_start(long long b, const Sched& s, int grid) { return b * s.work / grid; }
+// the CTA whose stream-K range holds k-block x of the flattened work
+__device__ __forceinline__ int sk_owner(long long x, const Sched& s, int grid) {
+  return static_cast<int>(((x + 1) * grid + s.work - 1) / s.work) - 1;
+}
+
+struct SegWalk {
+  long long x, end;
+  int u, grid;
+  bool first;
+  __device__ __forceinline__ SegWalk(const Sched& s, int b, int g) : u(b), grid(g), first(true) {
+    x = s.mode == 1 ? sk_start(b, s, g) : 0;
+    end = s.mode == 1 ? sk_start(b + 1, s, g) : 0;
+  }
+  __device__ __forceinline__ bool next(const Sched& s, Seg& sg) {
+    if (s.mode == 0) {
+      if (u >= s.units) return false;
+      sg.split = u % s.splits;
+      sg.t = u / s.splits;
+      sg.k0 = sg.split * s.kb_per_split;
+      sg.nkb = min(s.kb_per_split, s.kblocks - sg.k0);
+      u += grid;
+      return true;
+    }
+    if (x >= end) return false;
+    const long long kb = s.kblocks;
+    sg.t = static_cast<int>(x / kb);
+    const long long tile0 = static_cast<long long>(sg.t) * kb;
+    sg.k0 = static_cast<int>(x - tile0);
+    sg.nkb = static_cast<int>(min(kb, end - tile0)) - sg.k0;
+    sg.split = first ? 0 : 1;
+    first = false;
+    x = tile0 + sg.k0 + sg.nkb;
+    return true;
+  }
 };
 
 enum PersistentWaitSite : int {
@@ -147,14 +236,16 @@ enum PersistentWaitSite : int {
 };
 
 template <int BM, bool BF16>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(512, 1)
     w8a16_persistent_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                             const void* __restrict__ scale, int sdtype, void* __restrict__ y, int64_t ldy, int M,
-                            int N, int n_tiles, int kblocks, int kb_per_split, int splits, int units,
-                            float* __restrict__ ws, int* __restrict__ counters, const GatherArgs g) {
+                            int N, const Sched sc, float* __restrict__ ws, int* __restrict__ counters,
+                            const GatherArgs g) {
   using C = PCfg<BM>;
   constexpr int STAGES = C::STAGES;
   constexpr int ASTAGES = C::ASTAGES;
+  constexpr int NI = C::NI;
+  constexpr int DBUF = C::DBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem + C::OFF_W;
@@ -167,7 +258,8 @@ __global__ void __launch_bounds__(448, 1)
   uint64_t* dempty = dfull + 2;          // 2
   uint64_t* final_bar = dempty + 2;      // 1
   uint64_t* xfull = final_bar + 1;       // STAGES: the x tiles of a stage (full[] covers its W tile)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + STAGES);
+  uint64_t* xempty = xfull + STAGES;     // STAGES: the MMAs that read a stage's x tiles are done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket = abort_flag + 1;
 
@@ -178,17 +270,18 @@ __global__ void __launch_bounds__(448, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&xfull[s], 1);
-      mbar_init(&empty[s], 4 + 1);  // one group of 4 dequantiser warps + 1 MMA commit
+      mbar_init(&empty[s], 4);       // W tile read into registers by one group of 4 dequantiser warps
+      mbar_init(&xempty[s], NI);     // x tiles: a commit per issuer
     }
     for (int t = 0; t < ASTAGES; ++t) {
       mbar_init(&afull[t], 4);
-      mbar_init(&aempty[t], 1);
+      mbar_init(&aempty[t], NI);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&dfull[b], 1);
+    for (int b = 0; b < DBUF; ++b) {
+      mbar_init(&dfull[b], NI);
       mbar_init(&dempty[b], 4);
     }
-    mbar_init(final_bar, 1);
+    mbar_init(final_bar, NI);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -207,90 +300,75 @@ __global__ void __launch_bounds__(448, 1)
   if (threadIdx.x == 0) pdl_launch_dependents();
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer: weight tiles ----------------
+    // Weights do not depend on the preceding kernel (no griddepcontrol.wait here), and a
+    // slot is free as soon as a dequantiser group has read it into registers.
     if (lane == 0) {
-      // a weight tile used by several M-tiles stays in L2 for the neighbours that share it
-      const int m_tiles = units / (n_tiles * splits);
-      const uint64_t pol_w = m_tiles > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
-      const uint64_t pol_x = l2_policy_evict_last();
-      // (unit, k-block) walk of this CTA
-      int u = blockIdx.x, i = 0;
-      auto unit_kb = [&](int uu, int& nt, int& mt, int& kb0, int& nkb) {
-        const int sp = uu % splits;
-        const int t = uu / splits;
-        // M-tile fastest: the units that share a weight tile are consecutive
-        const int m_tiles_u = units / (n_tiles * splits);
-        mt = t % m_tiles_u;
-        nt = t / m_tiles_u;
-        kb0 = sp * kb_per_split;
-        nkb = min(kb_per_split, kblocks - kb0);
-      };
-      // Weights do not depend on the preceding kernel: fill the ring with weight
-      // tiles first, then wait for the predecessor (PDL) before loading x.
-      int pre = 0;
-      {
-        int uu = u, ii = 0;
-        while (uu < units && pre < STAGES) {
-          int nt, mt, kb0, nkb;
-          unit_kb(uu, nt, mt, kb0, nkb);
-          mbar_arrive_expect_tx(&full[pre], C::W_BYTES);
-          tma_load_2d(sW + pre * C::W_BYTES, &tm_w, &full[pre], (kb0 + ii) * C::BK, nt * 128, pol_w);
-          ++pre;
-          if (++ii == nkb) {
-            ii = 0;
-            uu += gridDim.x;
-          }
-        }
-      }
-      pdl_wait();
+      // a weight tile used by several M-tiles stays in L2 for the CTAs that share it
+      const uint64_t pol_w = sc.m_tiles > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
       int it = 0;
       bool ok = true;
-      while (u < units && ok) {
-        int nt, mt, kb0, nkb;
-        unit_kb(u, nt, mt, kb0, nkb);
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        const int kx = (kb0 + i) * C::BK;
-        if (it >= pre) {
-          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, kSitePProd)) {
+      SegWalk wk(sc, blockIdx.x, gridDim.x);
+      Seg sg;
+      while (ok && wk.next(sc, sg)) {
+        const int nt = sg.t / sc.m_tiles;
+        for (int i = 0; i < sg.nkb; ++i, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[s], C::W_BYTES);
-          tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], kx, nt * 128, pol_w);
-        }
-        mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
-        tma_load_2d(sX + s * C::X_BYTES, &tm_x, &xfull[s], kx, mt * BM, pol_x);
-        tma_load_2d(sX + s * C::X_BYTES + C::X_PANEL, &tm_x, &xfull[s], kx + 64, mt * BM, pol_x);
-        ++it;
-        if (++i == nkb) {
-          i = 0;
-          u += gridDim.x;
+          tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 128, pol_w);
         }
       }
-      if (!ok) {
+      if (!ok)  // wait (bounded) for the copies still in flight into this CTA's shared memory
         for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
-        {
           mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
-          mbar_wait(&xfull[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
+    }
+  } else if (warp == 15) {
+    // ---------------- TMA producer: activation tiles (after the predecessor) ----------------
+    if (lane == 0) {
+      const uint64_t pol_x = l2_policy_evict_last();
+      pdl_wait();
+      int it = 0;
+      bool ok = true;
+      SegWalk wk(sc, blockIdx.x, gridDim.x);
+      Seg sg;
+      while (ok && wk.next(sc, sg)) {
+        const int mt = sg.t % sc.m_tiles;
+        for (int i = 0; i < sg.nkb; ++i, ++it) {
+          const int s = it % STAGES;
+          const int kx = (sg.k0 + i) * C::BK;
+          if (it >= STAGES && !mbar_wait(&xempty[s], ((it / STAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
+          tma_load_2d(sX + s * C::X_BYTES, &tm_x, &xfull[s], kx, mt * BM, pol_x);
+          tma_load_2d(sX + s * C::X_BYTES + C::X_PANEL, &tm_x, &xfull[s], kx + 64, mt * BM, pol_x);
         }
       }
+      if (!ok)
+        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+          mbar_wait(&xfull[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 || (NI == 2 && warp == 14)) {
+    // ---------------- MMA issuers ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(128, BM, BF16, false);
+      constexpr int KK = 8 / NI;        // K=16 slices per k-block for each issuer
+      const int h = warp == 1 ? 0 : 1;  // issuer index
       int it = 0, j = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
-        const int sp = u % splits;
-        const int kb0 = sp * kb_per_split;
-        const int nkb = min(kb_per_split, kblocks - kb0);
-        const int b = j & 1;
-        if (!mbar_wait(&dempty[b], ((j >> 1) & 1) ^ 1, abort_flag, kSitePMmaD)) break;
+      SegWalk wk(sc, blockIdx.x, gridDim.x);
+      Seg sg;
+      for (; ok && wk.next(sc, sg); ++j) {
+        const int b = j % DBUF;
+        if (!mbar_wait(&dempty[b], ((j / DBUF) & 1) ^ 1, abort_flag, kSitePMmaD)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + C::D_COL0 + b * BM;
-        for (int i = 0; i < nkb; ++i, ++it) {
+        const uint32_t d_tmem = tmem + C::D_COL0 + (b * NI + h) * BM;
+        for (int i = 0; i < sg.nkb; ++i, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           const int t = it % ASTAGES;
@@ -302,11 +380,12 @@ __global__ void __launch_bounds__(448, 1)
           tc_fence_after();
           const uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int k2 = 0; k2 < KK; ++k2) {
+            const int kk = h * KK + k2;
             const uint64_t bd = make_sdesc(x_base + (kk >> 2) * C::X_PANEL + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-            umma_f16_ts(d_tmem, tmem + C::A_COL0 + t * 64 + kk * 8, bd, idesc, (i | kk) != 0 ? 1u : 0u);
+            umma_f16_ts(d_tmem, tmem + C::A_COL0 + t * 64 + kk * 8, bd, idesc, (i | k2) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          umma_commit(&xempty[s]);
           umma_commit(&aempty[t]);
         }
         if (ok) umma_commit(&dfull[b]);
@@ -326,55 +405,56 @@ __global__ void __launch_bounds__(448, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::A_COL0;
     int it = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const int sp = u % splits;
-      const int kb0 = sp * kb_per_split;
-      const int nkb = min(kb_per_split, kblocks - kb0);
-      for (int i = 0; i < nkb; ++i, ++it) {
+    SegWalk wk(sc, blockIdx.x, gridDim.x);
+    Seg sg;
+    while (ok && wk.next(sc, sg)) {
+      for (int i = 0; i < sg.nkb; ++i, ++it) {
         if ((it & 1) != grp) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         const int t = it % ASTAGES;
         const uint32_t pa = (it / ASTAGES) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag, kSitePConvFull) ||
-            !mbar_wait(&aempty[t], pa ^ 1, abort_flag, kSitePConvA)) {
+        if (!mbar_wait(&full[s], ph, abort_flag, kSitePConvFull)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = sW + s * C::W_BYTES + row * 128;
+        uint32_t out[2][32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
+          uint4 o0, o1;
+          convert_chunk<BF16>(v, o0, o1);
+          uint32_t* o = &out[c >> 2][8 * (c & 3)];
+          o[0] = o0.x;
+          o[1] = o0.y;
+          o[2] = o0.z;
+          o[3] = o0.w;
+          o[4] = o1.x;
+          o[5] = o1.y;
+          o[6] = o1.z;
+          o[7] = o1.w;
+        }
+        // The weight slot is free once the whole warp has converted its rows: the converted
+        // values depend on every byte read, so the reads are complete before the release (an
+        // arrive right after the loads let a fast L2 refill land under reads still in flight).
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (!mbar_wait(&aempty[t], pa ^ 1, abort_flag, kSitePConvA)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint8_t* src = sW + s * C::W_BYTES + row * 128;
-        uint4 v[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t out[32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint4 o0, o1;
-            convert_chunk<BF16>(v[4 * h + c], o0, o1);
-            out[8 * c + 0] = o0.x;
-            out[8 * c + 1] = o0.y;
-            out[8 * c + 2] = o0.z;
-            out[8 * c + 3] = o0.w;
-            out[8 * c + 4] = o1.x;
-            out[8 * c + 5] = o1.y;
-            out[8 * c + 6] = o1.z;
-            out[8 * c + 7] = o1.w;
-          }
-          tmem_st32(lane_base + t * 64 + h * 32, out);
-        }
+        tmem_st32(lane_base + t * 64, out[0]);
+        tmem_st32(lane_base + t * 64 + 32, out[1]);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&afull[t]);
-          mbar_arrive(&empty[s]);
-        }
+        if (lane == 0) mbar_arrive(&afull[t]);
       }
     }
-  } else {
-    // ---------------- epilogue ----------------
+  } else if (warp < 14) {
+    // ---------------- epilogue: warps 10-13 ----------------
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::D_COL0;
@@ -396,31 +476,46 @@ __global__ void __launch_bounds__(448, 1)
       gather_ok = !named_bar_any(1, 128, !gather_ok);
     }
     int j = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
-      const int sp = u % splits;
-      const int t = u / splits;
-      const int m_tiles_u = units / (n_tiles * splits);
-      const int mt = t % m_tiles_u;
-      const int nt = t / m_tiles_u;
+    SegWalk wk(sc, blockIdx.x, gridDim.x);
+    Seg sg;
+    for (; wk.next(sc, sg); ++j) {
+      const int t = sg.t;
+      const int nt = t / sc.m_tiles;
+      const int mt = t - nt * sc.m_tiles;
       const int n = nt * 128 + row;
       const int m0 = mt * BM;
-      const int b = j & 1;
-      const bool ok = mbar_wait(&dfull[b], (j >> 1) & 1, abort_flag, kSitePEpi);
+      const int b = j % DBUF;
+      const bool ok = mbar_wait(&dfull[b], (j / DBUF) & 1, abort_flag, kSitePEpi);
       if (named_bar_any(1, 128, !ok || *abort_flag)) break;  // same decision in all 4 warps
       tc_fence_after();
-      const uint32_t taddr = lane_addr + b * BM;
-      if (splits == 1) {
-        const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
+      const uint32_t taddr = lane_addr + b * NI * BM;
+      // 16 accumulator columns of this thread's row: issuer 0's sum plus issuer 1's
+      auto load_acc = [&](int c0, float (&v)[16]) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c0, r);
+        if constexpr (NI == 2) {
+          uint32_t r1[16];
+          tmem_ld16(taddr + BM + c0, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]) + __uint_as_float(r1[e]);
+        } else {
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
+        }
+      };
+      if (sg.nkb == sc.kblocks) {  // this CTA computes the tile's full K
+        const float scl = n < N ? load_as_float(scale, n, sdtype) : 0.f;
 #pragma unroll 1
         for (int c0 = 0; c0 < BM; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c0, r);
-          tmem_ld_wait();
+          float v[16];
+          load_acc(c0, v);
           if (n < N) {
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int m = m0 + c0 + e;
-              if (m < M) store_y<BF16>(y, g, ldy, m, n, __uint_as_float(r[e]) * sc);
+              if (m < M) store_y<BF16>(y, g, ldy, m, n, v[e] * scl);
             }
           }
         }
@@ -428,50 +523,68 @@ __global__ void __launch_bounds__(448, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&dempty[b]);
       } else {
-        float* mine = ws + (static_cast<size_t>(t) * splits + sp) * (128 * BM) + static_cast<size_t>(row) * BM;
+        // piece slots: [tile][split] (mode 0) or [cta][first/last segment] (mode 1)
+        const long long kb = sc.kblocks;
+        const int c_first = sc.mode == 0 ? 0 : sk_owner(t * kb, sc, gridDim.x);
+        const int n_parts = sc.mode == 0 ? sc.splits : sk_owner(t * kb + kb - 1, sc, gridDim.x) - c_first + 1;
+        auto part = [&](int c) -> float* {
+          size_t slot;
+          if (sc.mode == 0) {
+            slot = static_cast<size_t>(t) * sc.splits + c;
+          } else {
+            const long long cta = c_first + c;
+            slot = static_cast<size_t>(cta) * 2 + (sk_start(cta, sc, gridDim.x) / kb == t ? 0 : 1);
+          }
+          return ws + slot * (128 * BM) + static_cast<size_t>(row) * BM;
+        };
+        // tile counter: the tile itself (mode 0) or the CTA holding its first k-block, which
+        // heads at most one cut tile (mode 1); either way an index below kGemmCounterSlots
+        const int cidx = sc.mode == 0 ? t : c_first;
+        float* mine = sc.mode == 0 ? part(sg.split)
+                                   : ws + (static_cast<size_t>(blockIdx.x) * 2 + sg.split) * (128 * BM) +
+                                         static_cast<size_t>(row) * BM;
 #pragma unroll 1
         for (int c0 = 0; c0 < BM; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c0, r);
-          tmem_ld_wait();
+          float v[16];
+          load_acc(c0, v);
 #pragma unroll
           for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(mine + c0 + e) = make_float4(
-                __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+            *reinterpret_cast<float4*>(mine + c0 + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&dempty[b]);  // accumulator free; partials are in global memory
+        if (lane == 0) mbar_arrive(&dempty[b]);  // accumulator free; the piece is in global memory
         __threadfence();
         named_bar_sync(1, 128);
-        if (warp == 10 && lane == 0) *ticket = atomicAdd(&counters[t], 1);
+        if (warp == 10 && lane == 0) *ticket = atomicAdd(&counters[cidx], 1);
         named_bar_sync(1, 128);
-        const bool last = *ticket == splits - 1;
-        named_bar_sync(1, 128);  // every thread has read the ticket before the next unit overwrites it
+        const bool last = *ticket == n_parts - 1;
+        named_bar_sync(1, 128);  // every thread has read the ticket before the next segment overwrites it
         if (last) {
           __threadfence();
-          const float sc = n < N ? load_as_float(scale, n, sdtype) : 0.f;
-          const float* base = ws + static_cast<size_t>(t) * splits * (128 * BM) + static_cast<size_t>(row) * BM;
-          // 8 columns at a time; the loads of four partials are issued together, then
-          // summed in split order (partial 0 first, as the result must not depend on timing)
+          const float scl = n < N ? load_as_float(scale, n, sdtype) : 0.f;
+          // 16 columns at a time; the loads of four pieces (16 x 16 B per thread) are
+          // issued together, so a decode tile of up to four pieces is one L2 round trip,
+          // then summed in k order (piece 0 first, as the result must not depend on timing)
 #pragma unroll 1
-          for (int c0 = 0; c0 < BM; c0 += 8) {
-            float a[8];
+          for (int c0 = 0; c0 < BM; c0 += 16) {
+            float a[16];
 #pragma unroll 1
-            for (int p0 = 0; p0 < splits; p0 += 4) {
-              float4 v[4][2];
-#pragma unroll
-              for (int pp = 0; pp < 4; ++pp)
-#pragma unroll
-                for (int e = 0; e < 2; ++e)
-                  v[pp][e] = p0 + pp < splits ? __ldcg(reinterpret_cast<const float4*>(
-                                                    base + static_cast<size_t>(p0 + pp) * 128 * BM + c0 + 4 * e))
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p0 = 0; p0 < n_parts; p0 += 4) {
+              float4 v[4][4];
 #pragma unroll
               for (int pp = 0; pp < 4; ++pp) {
-                if (p0 + pp >= splits) break;
+                const float* src = p0 + pp < n_parts ? part(p0 + pp) : nullptr;
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
+                for (int e = 0; e < 4; ++e)
+                  v[pp][e] = src ? __ldcg(reinterpret_cast<const float4*>(src + c0 + 4 * e))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int pp = 0; pp < 4; ++pp) {
+                if (p0 + pp >= n_parts) break;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
                   const float f[4] = {v[pp][e].x, v[pp][e].y, v[pp][e].z, v[pp][e].w};
 #pragma unroll
                   for (int g = 0; g < 4; ++g) a[4 * e + g] = (p0 + pp == 0) ? f[g] : a[4 * e + g] + f[g];
@@ -480,13 +593,13 @@ __global__ void __launch_bounds__(448, 1)
             }
             if (n < N) {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
+              for (int e = 0; e < 16; ++e) {
                 const int m = m0 + c0 + e;
-                if (m < M) store_y<BF16>(y, g, ldy, m, n, a[e] * sc);
+                if (m < M) store_y<BF16>(y, g, ldy, m, n, a[e] * scl);
               }
             }
           }
-          if (warp == 10 && lane == 0) counters[t] = 0;
+          if (warp == 10 && lane == 0) counters[cidx] = 0;
         }
       }
     }
@@ -541,12 +654,17 @@ __global__ void __launch_bounds__(128) w8a16_simt_kernel(const void* __restrict_
 struct GemmPlan {
   int bm = 16;
   int n_tiles = 0, m_tiles = 0, kblocks = 0, splits = 1, kb_per_split = 0, units = 0, grid = 0;
+  int mode = 0;         // 0: split-K units, 1: stream-K ranges
+  long long work = 0;   // tiles * kblocks
   size_t counter_bytes = 0, partial_bytes = 0;
 };
 
-// Persistent path: pick the split count that minimises the busiest CTA's work,
-// counting each k-block as 16 KB of weights and each unit a fixed overhead
-// (epilogue, pipeline hand-off) plus, when split, its fp32 partial round trip.
+// Persistent path.  Cost model: the busiest CTA's work, counting each k-block as
+// 16 KB of weights, each unit or segment a fixed overhead (epilogue, pipeline
+// hand-off) and each fp32 piece written a round trip.  Split-K (mode 0) picks
+// the split count; when CTAs would walk several units each, stream-K (mode 1)
+// removes the last round's imbalance (e.g. 1187 LM-head tiles on 148 SMs:
+// 9 units for some CTAs against 8.02 on average).
 static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k) {
   GemmPlan p;
   const int sms = num_sms();
@@ -555,28 +673,58 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k) {
   p.bm = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
   p.m_tiles = static_cast<int>((m + p.bm - 1) / p.bm);
   const int64_t tiles = static_cast<int64_t>(p.n_tiles) * p.m_tiles;
-  // split-K count: cost model over the units each CTA walks (weight bytes per unit,
-  // a fixed per-unit cost, the partials a split writes)
+  const double part_cost = 2.0 * 128 * p.bm * 4;
   double best = 1e300;
+  int64_t best_per_cta = 1;
   for (int sp = 1; sp <= p.kblocks && sp <= 32; ++sp) {
     const int kbps = (p.kblocks + sp - 1) / sp;
     const int real = (p.kblocks + kbps - 1) / kbps;
     if (real != sp) continue;
     const int64_t units = tiles * sp;
     const int64_t per_cta = (units + sms - 1) / sms;
-    const double unit_cost = kbps * 16384.0 + 6000.0 + (sp > 1 ? 2.0 * 128 * p.bm * 4 : 0.0);
+    const double unit_cost = kbps * 16384.0 + 6000.0 + (sp > 1 ? part_cost : 0.0);
     const double cost = static_cast<double>(per_cta) * unit_cost;
     if (cost < best * 0.97) {
       best = cost;
+      best_per_cta = per_cta;
       p.splits = sp;
       p.kb_per_split = kbps;
+    }
+  }
+  p.work = tiles * p.kblocks;
+  // split-K counters are per tile: more split tiles than counter slots go to stream-K
+  const bool force_sk = p.splits > 1 && tiles > kGemmCounterSlots;
+  if ((best_per_cta >= 2 || force_sk) && p.work >= sms && tiles <= INT32_MAX && p.work < (1LL << 40)) {
+    const int64_t per = (p.work + sms - 1) / sms;
+    const double seg = static_cast<double>((per + p.kblocks - 1) / p.kblocks + 1);
+    const double cost = per * 16384.0 + seg * 6000.0 + 2.0 * part_cost;
+    if (cost < best || force_sk) {
+      p.mode = 1;
+      p.grid = sms;
+      p.splits = 1;
+      p.kb_per_split = p.kblocks;
+      p.units = 0;
+      bool cut = false;  // does a range boundary fall inside a tile?
+      for (int b = 1; b < sms && !cut; ++b) cut = (static_cast<int64_t>(b) * p.work / sms) % p.kblocks != 0;
+      if (cut) {
+        p.counter_bytes = kGemmCounterBytes;
+        p.partial_bytes = static_cast<size_t>(sms) * 2 * 128 * p.bm * sizeof(float);
+      }
+      return p;
     }
   }
   const int64_t units = tiles * p.splits;
   p.units = units > INT32_MAX ? -1 : static_cast<int>(units);  // -1: too many units (refused by the caller)
   p.grid = units < sms ? static_cast<int>(units) : sms;
   if (p.splits > 1) {
-    p.counter_bytes = ((static_cast<size_t>(tiles) * sizeof(int) + 255) / 256) * 256;
+    if (tiles > kGemmCounterSlots) {  // unreachable for realistic shapes: work < sms with > 1024 tiles
+      p.splits = 1;
+      p.kb_per_split = p.kblocks;
+      p.units = tiles > INT32_MAX ? -1 : static_cast<int>(tiles);
+      p.grid = tiles < sms ? static_cast<int>(tiles) : sms;
+      return p;
+    }
+    p.counter_bytes = kGemmCounterBytes;
     p.partial_bytes = static_cast<size_t>(tiles) * p.splits * 128 * p.bm * sizeof(float);
   }
   return p;
@@ -608,8 +756,17 @@ static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = g_use_pdl ? 1 : 0;
-  return check_cuda(cudaLaunchKernelEx(&cfg, w8a16_persistent_kernel<BM, BF16>, tw, tx, scale, sdt, y, ldy, M, N,
-                                       p.n_tiles, p.kblocks, p.kb_per_split, p.splits, p.units, ws, counters, g),
+  Sched sc;
+  sc.mode = p.mode;
+  sc.n_tiles = p.n_tiles;
+  sc.m_tiles = p.m_tiles;
+  sc.kblocks = p.kblocks;
+  sc.splits = p.splits;
+  sc.kb_per_split = p.kb_per_split;
+  sc.units = p.units;
+  sc.work = p.work;
+  return check_cuda(cudaLaunchKernelEx(&cfg, w8a16_persistent_kernel<BM, BF16>, tw, tx, scale, sdt, y, ldy, M, N, sc,
+                                       ws, counters, g),
                     "cudaLaunchKernelEx(w8a16_persistent_kernel)");
 }
 
@@ -678,7 +835,7 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
                                (long long)m, (long long)n);
   float* ws = nullptr;
   int* counters = nullptr;
-  if (p.splits > 1) {
+  if (p.partial_bytes > 0) {
     if (workspace == nullptr || workspace_bytes < p.counter_bytes + p.partial_bytes)
       return fail(BW_ERR_WORKSPACE, "int8_gemm: workspace of %zu bytes required, %zu given",
                   p.counter_bytes + p.partial_bytes, workspace_bytes);

@@ -64,7 +64,9 @@ int bw_quantize_rowwise_int8(const void* w, int w_dtype, int64_t n, int64_t k, i
  *   y      [m, n] x_dtype, row stride ldy
  *   workspace: device memory of bw_w8a16_gemm_workspace_size() bytes whose
  *   first bw_w8a16_gemm_workspace_zeroed_bytes() bytes are zero before the
- *   first call (split-K tile counters; every successful call leaves them zero).
+ *   first call (split-K / stream-K tile counters; every successful call leaves
+ *   them zero).  The zeroed prefix has the same size for every shape, so one
+ *   workspace sized for the largest shape serves calls of any shapes.
  * Calls that share a workspace must not overlap on the GPU.
  */
 size_t bw_w8a16_gemm_workspace_size(int64_t m, int64_t n, int64_t k);

@@ -132,6 +132,68 @@ def test_gemm_deterministic_and_reusable(cuda_dev, ops):
         assert torch.equal(y, ys[0])
 
 
+@pytest.mark.parametrize("m,n,k", [(16, 8192, 28672), (1, 1024, 28672), (64, 3072, 8192), (16, 28672, 8192),
+                                   (130, 2048, 8192)])
+def test_gemm_stream_k_cut_tiles(m, n, k, cuda_dev):
+    """Shapes whose tiles are cut between several CTAs' k-ranges (stream-K): parity,
+    bit-identical repeats through the C ABI with one workspace, counters back to zero."""
+    from blackwell_ops import _lib
+
+    lib = _lib.lib
+    g = torch.Generator(device=cuda_dev).manual_seed(m + n + k)
+    w = (torch.randn(n, k, generator=g, device=cuda_dev) * 0.02).to(torch.bfloat16)
+    from blackwell_ops.kernels import quantize_weight_int8
+
+    q, s = quantize_weight_int8(w)
+    x = torch.randn(m, k, generator=g, device=cuda_dev).to(torch.bfloat16)
+    need = lib.bw_w8a16_gemm_workspace_size(m, n, k)
+    ws = torch.zeros(max(need, 16), dtype=torch.uint8, device=cuda_dev)
+    st = _lib.stream_ptr(cuda_dev)
+    ys = []
+    for _ in range(3):
+        y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda_dev)
+        rc = lib.bw_w8a16_gemm(x.data_ptr(), 1, k, q.data_ptr(), k, s.data_ptr(), 1, y.data_ptr(), n, m, n, k,
+                               ws.data_ptr(), ws.numel(), st)
+        assert rc == 0, lib.bw_last_error()
+        ys.append(y)
+    torch.cuda.synchronize()
+    ref = x.double() @ (q.double() * s.double()[:, None]).t()
+    err = (ys[0].double() - ref).abs()
+    assert bool((err <= 1e-2 + 2.0 ** -8 * ref.abs()).all()), float(err.max())
+    assert all(torch.equal(y, ys[0]) for y in ys[1:])
+    zeroed = lib.bw_w8a16_gemm_workspace_zeroed_bytes(m, n, k)
+    assert int(ws[:zeroed].sum()) == 0
+    assert _lib.device_status() == 0
+
+
+def test_gemm_workspace_shared_across_shapes(cuda_dev):
+    """One workspace serves a sequence of shapes with different plans (split-K, stream-K,
+    cut tiles): each call's pieces never land on another shape's counters."""
+    from blackwell_ops import _lib
+
+    lib = _lib.lib
+    shapes = [(16, 3072, 1024), (16, 151936, 1024), (1, 1024, 28672), (16, 3072, 1024), (64, 3072, 8192),
+              (16, 151936, 1024)]
+    need = max(lib.bw_w8a16_gemm_workspace_size(*sh) for sh in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda_dev)
+    st = _lib.stream_ptr(cuda_dev)
+    g = torch.Generator(device=cuda_dev).manual_seed(11)
+    for m, n, k in shapes:
+        q = torch.randint(-127, 128, (n, k), generator=g, device=cuda_dev, dtype=torch.int8)
+        # scales keep |y| in the range where the absolute fp16 bound is meaningful (|y| < 8)
+        s = ((torch.rand(n, generator=g, device=cuda_dev) * 1e-3 + 1e-4) * (1024.0 / k) ** 0.5).half()
+        x = torch.randn(m, k, generator=g, device=cuda_dev).half()
+        y = torch.full((m, n), float("nan"), dtype=torch.float16, device=cuda_dev)
+        rc = lib.bw_w8a16_gemm(x.data_ptr(), 0, k, q.data_ptr(), k, s.data_ptr(), 0, y.data_ptr(), n, m, n, k,
+                               ws.data_ptr(), ws.numel(), st)
+        assert rc == 0, lib.bw_last_error()
+        ref = x.double() @ (q.double() * s.double()[:, None]).t()
+        err = (y.double() - ref).abs()
+        assert float(err.max()) <= 1e-2 and float(err.norm() / ref.norm()) <= 1e-3, (m, n, k)
+    assert int(ws[: lib.bw_w8a16_gemm_workspace_zeroed_bytes(16, 151936, 1024)].sum()) == 0
+    assert _lib.device_status() == 0
+
+
 @pytest.mark.parametrize("m,n,k", [(2048, 14336, 4096), (512, 4096, 14336), (4096, 8192, 2048)])
 def test_gemm_prefill_full_size_vs_torch_fp32(m, n, k, cuda_dev, ops):
     """Full prefill sizes: compared with torch's fp32 dequantise-matmul on the GPU (TF32 off)."""
