@@ -120,6 +120,9 @@ __device__ __forceinline__ void store_y(void* y, const GatherArgs& g, int64_t ld
 #ifndef BW_GEMM_SMALL_ISSUERS
 #define BW_GEMM_SMALL_ISSUERS 2
 #endif
+#ifndef BW_GEMM_STREAMK
+#define BW_GEMM_STREAMK 1
+#endif
 #ifndef BW_GEMM_BM128_ISSUERS
 #define BW_GEMM_BM128_ISSUERS 1
 #endif
@@ -184,19 +187,26 @@ struct Seg {
   int t, k0, nkb, split;  // split: k-split index (mode 0); 0 = first / 1 = later segment of the CTA (mode 1)
 };
 
-__device__ __forceinline__ long long sk_start(long long b, const Sched& s, int grid) { return b * s.work / grid; }
+// Stream-K plans keep work * grid below 2^31 (checked by the planner), so the
+// range arithmetic is 32-bit.
+__device__ __forceinline__ long long sk_start(long long b, const Sched& s, int grid) {
+  return static_cast<long long>(static_cast<unsigned>(b) * static_cast<unsigned>(s.work) / static_cast<unsigned>(grid));
+}
 // the CTA whose stream-K range holds k-block x of the flattened work
 __device__ __forceinline__ int sk_owner(long long x, const Sched& s, int grid) {
-  return static_cast<int>(((x + 1) * grid + s.work - 1) / s.work) - 1;
+  const unsigned w = static_cast<unsigned>(s.work);
+  return static_cast<int>((static_cast<unsigned>(x + 1) * static_cast<unsigned>(grid) + w - 1) / w) - 1;
 }
 
 struct SegWalk {
   long long x, end;
   int u, grid;
   bool first;
-  __device__ __forceinline__ SegWalk(const Sched& s, int b, int g) : u(b), grid(g), first(true) {
-    x = s.mode == 1 ? sk_start(b, s, g) : 0;
-    end = s.mode == 1 ? sk_start(b + 1, s, g) : 0;
+  __device__ __forceinline__ SegWalk(const Sched& s, int b, int g) : x(0), end(0), u(b), grid(g), first(true) {
+    if (s.mode == 1) {
+      x = sk_start(b, s, g);
+      end = sk_start(b + 1, s, g);
+    }
   }
   __device__ __forceinline__ bool next(const Sched& s, Seg& sg) {
     if (s.mode == 0) {
@@ -527,22 +537,27 @@ __global__ void __launch_bounds__(512, 1)
         const long long kb = sc.kblocks;
         const int c_first = sc.mode == 0 ? 0 : sk_owner(t * kb, sc, gridDim.x);
         const int n_parts = sc.mode == 0 ? sc.splits : sk_owner(t * kb + kb - 1, sc, gridDim.x) - c_first + 1;
-        auto part = [&](int c) -> float* {
-          size_t slot;
-          if (sc.mode == 0) {
-            slot = static_cast<size_t>(t) * sc.splits + c;
-          } else {
-            const long long cta = c_first + c;
-            slot = static_cast<size_t>(cta) * 2 + (sk_start(cta, sc, gridDim.x) / kb == t ? 0 : 1);
-          }
-          return ws + slot * (128 * BM) + static_cast<size_t>(row) * BM;
-        };
+        // piece c of the tile sits at base + c * stride (+ off0 for piece 0): in mode 1 every
+        // contributor after the first starts its range inside the tile (its slot 0), and only
+        // the first may hold the tile as its last segment (slot 1).  Branch-free addresses keep
+        // the reduction's loads of four pieces in flight together.
+        constexpr size_t kPiece = static_cast<size_t>(128) * BM;
+        const float* pbase;
+        size_t pstride, poff0 = 0;
+        if (sc.mode == 0) {
+          pbase = ws + static_cast<size_t>(t) * sc.splits * kPiece + static_cast<size_t>(row) * BM;
+          pstride = kPiece;
+        } else {
+          pbase = ws + static_cast<size_t>(c_first) * 2 * kPiece + static_cast<size_t>(row) * BM;
+          pstride = 2 * kPiece;
+          poff0 = sk_start(c_first, sc, gridDim.x) / kb == t ? 0 : kPiece;
+        }
         // tile counter: the tile itself (mode 0) or the CTA holding its first k-block, which
         // heads at most one cut tile (mode 1); either way an index below kGemmCounterSlots
         const int cidx = sc.mode == 0 ? t : c_first;
-        float* mine = sc.mode == 0 ? part(sg.split)
-                                   : ws + (static_cast<size_t>(blockIdx.x) * 2 + sg.split) * (128 * BM) +
-                                         static_cast<size_t>(row) * BM;
+        float* mine = ws + (sc.mode == 0 ? static_cast<size_t>(t) * sc.splits + sg.split
+                                         : static_cast<size_t>(blockIdx.x) * 2 + sg.split) * kPiece +
+                      static_cast<size_t>(row) * BM;
 #pragma unroll 1
         for (int c0 = 0; c0 < BM; c0 += 16) {
           float v[16];
@@ -563,28 +578,28 @@ __global__ void __launch_bounds__(512, 1)
         if (last) {
           __threadfence();
           const float scl = n < N ? load_as_float(scale, n, sdtype) : 0.f;
-          // 16 columns at a time; the loads of four pieces (16 x 16 B per thread) are
-          // issued together, so a decode tile of up to four pieces is one L2 round trip,
-          // then summed in k order (piece 0 first, as the result must not depend on timing)
+          // 8 columns at a time; the loads of four pieces are issued together, then summed
+          // in k order (piece 0 first, as the result must not depend on timing).  Issuing
+          // 16 columns of four pieces at once measured slower (register-bound load batching).
 #pragma unroll 1
-          for (int c0 = 0; c0 < BM; c0 += 16) {
-            float a[16];
+          for (int c0 = 0; c0 < BM; c0 += 8) {
+            float a[8];
 #pragma unroll 1
             for (int p0 = 0; p0 < n_parts; p0 += 4) {
-              float4 v[4][4];
+              float4 v[4][2];
 #pragma unroll
-              for (int pp = 0; pp < 4; ++pp) {
-                const float* src = p0 + pp < n_parts ? part(p0 + pp) : nullptr;
+              for (int pp = 0; pp < 4; ++pp)
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  v[pp][e] = src ? __ldcg(reinterpret_cast<const float4*>(src + c0 + 4 * e))
+                for (int e = 0; e < 2; ++e)
+                  v[pp][e] = p0 + pp < n_parts
+                                 ? __ldcg(reinterpret_cast<const float4*>(pbase + (p0 + pp) * pstride +
+                                                                          (p0 + pp == 0 ? poff0 : 0) + c0 + 4 * e))
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-              }
 #pragma unroll
               for (int pp = 0; pp < 4; ++pp) {
                 if (p0 + pp >= n_parts) break;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
+                for (int e = 0; e < 2; ++e) {
                   const float f[4] = {v[pp][e].x, v[pp][e].y, v[pp][e].z, v[pp][e].w};
 #pragma unroll
                   for (int g = 0; g < 4; ++g) a[4 * e + g] = (p0 + pp == 0) ? f[g] : a[4 * e + g] + f[g];
@@ -593,7 +608,7 @@ __global__ void __launch_bounds__(512, 1)
             }
             if (n < N) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
+              for (int e = 0; e < 8; ++e) {
                 const int m = m0 + c0 + e;
                 if (m < M) store_y<BF16>(y, g, ldy, m, n, a[e] * scl);
               }
@@ -694,7 +709,11 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k) {
   p.work = tiles * p.kblocks;
   // split-K counters are per tile: more split tiles than counter slots go to stream-K
   const bool force_sk = p.splits > 1 && tiles > kGemmCounterSlots;
-  if ((best_per_cta >= 2 || force_sk) && p.work >= sms && tiles <= INT32_MAX && p.work < (1LL << 40)) {
+  // prefill tiles (BM = 128) keep split-K units unless forced: measured 809 against 784 TFLOPS on
+  // the Llama-3-8B MLP, as the 64 KB pieces of cut tiles and their end-of-range reductions cost
+  // more than the last round's imbalance
+  if (BW_GEMM_STREAMK && ((best_per_cta >= 2 && p.bm < 128) || force_sk) && p.work >= sms &&
+      p.work * sms < (1LL << 31)) {
     const int64_t per = (p.work + sms - 1) / sms;
     const double seg = static_cast<double>((per + p.kblocks - 1) / p.kblocks + 1);
     const double cost = per * 16384.0 + seg * 6000.0 + 2.0 * part_cost;
