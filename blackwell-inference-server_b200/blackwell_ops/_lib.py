@@ -46,6 +46,9 @@ SIGNATURES = {
     "bw_w8a16_gemm_workspace_zeroed_bytes": (_c.c_size_t, [_I64, _I64, _I64]),
     "bw_w8a16_gemm": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64, _P,
                                  _c.c_size_t, _P]),
+    "bw_w8a16_gemm_swiglu_workspace_size": (_c.c_size_t, [_I64, _I64, _I64]),
+    "bw_w8a16_gemm_swiglu": (_c.c_int, [_P, _c.c_int, _I64, _P, _P, _I64, _P, _P, _c.c_int, _P, _I64, _I64, _I64,
+                                        _I64, _P, _c.c_size_t, _P]),
     "bw_w8a16_gemm_static_scratch_bytes": (_c.c_size_t, []),
     "bw_w8a16_gemm_noalloc": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
                                          _P]),

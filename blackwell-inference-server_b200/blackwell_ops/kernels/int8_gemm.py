@@ -126,3 +126,53 @@ def int8_gemm(x: torch.Tensor, w_int8: torch.Tensor, scale: torch.Tensor) -> tor
             "int8_gemm",
         )
     return y
+
+
+def int8_gemm_swiglu(x: torch.Tensor, w_gate: torch.Tensor, s_gate: torch.Tensor, w_up: torch.Tensor,
+                     s_up: torch.Tensor) -> torch.Tensor:
+    """Fused ``swiglu(int8_gemm(x, w_gate, s_gate), int8_gemm(x, w_up, s_up))`` in one launch.
+
+    The MLP's gate and up projections share x; one kernel streams both int8 weights, rounds each
+    product to x.dtype as int8_gemm would, and writes ``silu(g) * u`` (fp32 silu, as the reference
+    swiglu kernel, src/blackwell_ops/cuda/basic_ops.cu:112-122).  Same argument rules as int8_gemm;
+    w_gate and w_up are [N, K], s_gate and s_up [N] of one dtype.  Returns [M, N] in x.dtype.
+    """
+    if not all(t.is_cuda for t in (x, w_gate, s_gate, w_up, s_up)):
+        raise RuntimeError("int8_gemm_swiglu: all inputs must be CUDA tensors")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError(f"int8_gemm_swiglu: x must be fp16 or bf16, got {x.dtype}")
+    if w_gate.dtype != torch.int8 or w_up.dtype != torch.int8:
+        raise RuntimeError("int8_gemm_swiglu: w_gate and w_up must be int8")
+    if s_gate.dtype not in DTYPE_CODE or s_up.dtype != s_gate.dtype:
+        raise RuntimeError("int8_gemm_swiglu: s_gate and s_up must share one supported dtype")
+    if x.dim() != 2 or w_gate.dim() != 2 or w_up.shape != w_gate.shape:
+        raise RuntimeError("int8_gemm_swiglu: x must be [M, K], w_gate and w_up [N, K]")
+    M, K = x.shape
+    N = w_gate.shape[0]
+    if w_gate.shape[1] != K:
+        raise RuntimeError(f"int8_gemm_swiglu: K mismatch ({K} vs {w_gate.shape[1]})")
+    if s_gate.numel() != N or s_up.numel() != N:
+        raise RuntimeError(f"int8_gemm_swiglu: scales must have N={N} elements")
+    y = torch.empty(M, N, device=x.device, dtype=x.dtype)
+    if M == 0 or N == 0:
+        return y
+    if K == 0:
+        return y.zero_()
+    if x.stride(1) != 1 or x.stride(0) < K:
+        x = x.contiguous()
+    w_gate = w_gate.contiguous()
+    w_up = w_up.contiguous()
+    s_gate = s_gate.reshape(N).contiguous()
+    s_up = s_up.reshape(N).contiguous()
+    with torch.cuda.device(x.device):
+        st = stream_ptr(x.device)
+        nbytes = lib.bw_w8a16_gemm_swiglu_workspace_size(M, N, K)
+        ws = _workspace(x.device, st, nbytes)
+        check(
+            lib.bw_w8a16_gemm_swiglu(x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0), w_gate.data_ptr(),
+                                     w_up.data_ptr(), K, s_gate.data_ptr(), s_up.data_ptr(), DTYPE_CODE[s_gate.dtype],
+                                     y.data_ptr(), N, M, N, K, ws.data_ptr() if ws is not None else None,
+                                     ws.numel() if ws is not None else 0, st),
+            "int8_gemm_swiglu",
+        )
+    return y

@@ -19,6 +19,7 @@
 #include <stdio.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -89,6 +90,13 @@ __device__ __forceinline__ void store_y(void* y, const GatherArgs& g, int64_t ld
   }
 }
 
+// dt(v): the value an unfused int8_gemm would have written.
+template <bool BF16>
+__device__ __forceinline__ float round_out(float v) {
+  if constexpr (BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  else return __half2float(__float2half_rn(v));
+}
+
 // ---------------------------------------------------------------------------
 // Persistent W8A16 GEMM for every M (decode, prefill).
 //
@@ -146,7 +154,8 @@ struct PCfg {
   static constexpr int OFF_X = STAGES * W_BYTES;
   static constexpr int OFF_BAR = OFF_X + STAGES * X_BYTES;
   static constexpr int BAR_BYTES = 512;
-  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
+  static constexpr int OFF_XCH = OFF_BAR + BAR_BYTES;  // SwiGLU epilogue: 64 rows x 16 fp32 (4 KB)
+  static constexpr int SMEM = OFF_XCH + 4096 + 1024;
   static constexpr int THREADS = 512;
   static_assert(BM >= 16 && BM <= 128 && BM % 16 == 0, "UMMA N for M=128");
   static_assert(NI == 1 || NI == 2, "one or two MMA issuers");
@@ -245,10 +254,18 @@ enum PersistentWaitSite : int {
   kSiteGDone = 131,
 };
 
-template <int BM, bool BF16>
+// GLU = true: the fused gate/up + SwiGLU variant.  A tile is 64 rows of the gate
+// weight and the same 64 rows of the up weight (two 64-row TMA boxes stacked into
+// one 128-row stage, so both weights keep the reference's layout); the epilogue's
+// up-row warps hand their dt-rounded values to the gate-row warps through shared
+// memory, which write y = dt(silu(g) * u) for 64 output columns:
+// swiglu(int8_gemm(x, w_gate, s_gate), int8_gemm(x, w_up, s_up)) in one launch
+// (reference swiglu_kernel, src/blackwell_ops/cuda/basic_ops.cu:112-122).
+template <int BM, bool BF16, bool GLU>
 __global__ void __launch_bounds__(512, 1)
-    w8a16_persistent_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                            const void* __restrict__ scale, int sdtype, void* __restrict__ y, int64_t ldy, int M,
+    w8a16_persistent_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
+                            const __grid_constant__ CUtensorMap tm_x, const void* __restrict__ scale,
+                            const void* __restrict__ scale2, int sdtype, void* __restrict__ y, int64_t ldy, int M,
                             int N, const Sched sc, float* __restrict__ ws, int* __restrict__ counters,
                             const GatherArgs g) {
   using C = PCfg<BM>;
@@ -297,6 +314,7 @@ __global__ void __launch_bounds__(512, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
+    if (GLU) tma_prefetch_desc(&tm_w2);
     tma_prefetch_desc(&tm_x);
   }
   if (warp == 1) {
@@ -329,7 +347,12 @@ __global__ void __launch_bounds__(512, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], C::W_BYTES);
-          tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 128, pol_w);
+          if constexpr (GLU) {
+            tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 64, pol_w);
+            tma_load_2d(sW + s * C::W_BYTES + C::W_BYTES / 2, &tm_w2, &full[s], (sg.k0 + i) * C::BK, nt * 64, pol_w);
+          } else {
+            tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 128, pol_w);
+          }
         }
       }
       if (!ok)  // wait (bounded) for the copies still in flight into this CTA's shared memory
@@ -468,6 +491,7 @@ __global__ void __launch_bounds__(512, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::D_COL0;
+    float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH);
     pdl_wait();
     bool gather_ok = true;
     uint32_t epoch = 0;
@@ -492,8 +516,9 @@ __global__ void __launch_bounds__(512, 1)
       const int t = sg.t;
       const int nt = t / sc.m_tiles;
       const int mt = t - nt * sc.m_tiles;
-      const int n = nt * 128 + row;
+      const int n = GLU ? nt * 64 + (row & 63) : nt * 128 + row;
       const int m0 = mt * BM;
+      const void* srow = GLU && row >= 64 ? scale2 : scale;
       const int b = j % DBUF;
       const bool ok = mbar_wait(&dfull[b], (j / DBUF) & 1, abort_flag, kSitePEpi);
       if (named_bar_any(1, 128, !ok || *abort_flag)) break;  // same decision in all 4 warps
@@ -515,19 +540,46 @@ __global__ void __launch_bounds__(512, 1)
           for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
         }
       };
+      // Output of CH consecutive tokens [c0, c0 + CH) of this thread's row, already scaled.
+      // SwiGLU: up rows (warps of lane quarters 2, 3) pass dt(up) through shared memory; gate
+      // rows write dt(silu(dt(gate)) * dt(up)).  Every epilogue thread calls this (barriers).
+      auto emit = [&](const float* v, int c0, auto ch_tag) {
+        constexpr int CH = decltype(ch_tag)::value;
+        if constexpr (!GLU) {
+          if (n < N) {
+#pragma unroll
+            for (int e = 0; e < CH; ++e) {
+              const int m = m0 + c0 + e;
+              if (m < M) store_y<BF16>(y, g, ldy, m, n, v[e]);
+            }
+          }
+        } else {
+          if (row >= 64) {
+#pragma unroll
+            for (int e = 0; e < CH; ++e) xch[(row - 64) * 16 + e] = round_out<BF16>(v[e]);
+          }
+          named_bar_sync(1, 128);
+          if (row < 64 && n < N) {
+#pragma unroll
+            for (int e = 0; e < CH; ++e) {
+              const int m = m0 + c0 + e;
+              const float gt = round_out<BF16>(v[e]);
+              const float up = xch[row * 16 + e];
+              if (m < M) store_y<BF16>(y, g, ldy, m, n, gt / (1.0f + expf(-gt)) * up);
+            }
+          }
+          named_bar_sync(1, 128);  // the buffer is read before the next chunk overwrites it
+        }
+      };
       if (sg.nkb == sc.kblocks) {  // this CTA computes the tile's full K
-        const float scl = n < N ? load_as_float(scale, n, sdtype) : 0.f;
+        const float scl = n < N ? load_as_float(srow, n, sdtype) : 0.f;
 #pragma unroll 1
         for (int c0 = 0; c0 < BM; c0 += 16) {
           float v[16];
           load_acc(c0, v);
-          if (n < N) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int m = m0 + c0 + e;
-              if (m < M) store_y<BF16>(y, g, ldy, m, n, v[e] * scl);
-            }
-          }
+          for (int e = 0; e < 16; ++e) v[e] *= scl;
+          emit(v, c0, std::integral_constant<int, 16>{});
         }
         tc_fence_before();
         __syncwarp();
@@ -577,7 +629,7 @@ __global__ void __launch_bounds__(512, 1)
         named_bar_sync(1, 128);  // every thread has read the ticket before the next segment overwrites it
         if (last) {
           __threadfence();
-          const float scl = n < N ? load_as_float(scale, n, sdtype) : 0.f;
+          const float scl = n < N ? load_as_float(srow, n, sdtype) : 0.f;
           // 8 columns at a time; the loads of four pieces are issued together, then summed
           // in k order (piece 0 first, as the result must not depend on timing).  Issuing
           // 16 columns of four pieces at once measured slower (register-bound load batching).
@@ -606,13 +658,9 @@ __global__ void __launch_bounds__(512, 1)
                 }
               }
             }
-            if (n < N) {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const int m = m0 + c0 + e;
-                if (m < M) store_y<BF16>(y, g, ldy, m, n, a[e] * scl);
-              }
-            }
+            for (int e = 0; e < 8; ++e) a[e] *= scl;
+            emit(a, c0, std::integral_constant<int, 8>{});
           }
           if (warp == 10 && lane == 0) counters[cidx] = 0;
         }
@@ -663,6 +711,30 @@ __global__ void __launch_bounds__(128) w8a16_simt_kernel(const void* __restrict_
   store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, acc * load_as_float(scale, n, sdtype));
 }
 
+// CUDA-core fallback of the fused gate/up + SwiGLU op: one thread per output.
+template <bool BF16>
+__global__ void __launch_bounds__(128) w8a16_swiglu_simt_kernel(const void* __restrict__ x, int64_t ldx,
+                                                                const int8_t* __restrict__ wg,
+                                                                const int8_t* __restrict__ wu, int64_t ldw,
+                                                                const void* __restrict__ sg,
+                                                                const void* __restrict__ su, int sdtype,
+                                                                void* __restrict__ y, int64_t ldy, int M, int N,
+                                                                int K) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = blockIdx.y;
+  if (n >= N || m >= M) return;
+  const int xdt = BF16 ? BW_DTYPE_BF16 : BW_DTYPE_F16;
+  float ag = 0.f, au = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const float xv = load_as_float(x, static_cast<int64_t>(m) * ldx + k, xdt);
+    ag = fmaf(xv, static_cast<float>(wg[static_cast<int64_t>(n) * ldw + k]), ag);
+    au = fmaf(xv, static_cast<float>(wu[static_cast<int64_t>(n) * ldw + k]), au);
+  }
+  const float gt = round_out<BF16>(ag * load_as_float(sg, n, sdtype));
+  const float up = round_out<BF16>(au * load_as_float(su, n, sdtype));
+  store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, gt / (1.0f + expf(-gt)) * up);
+}
+
 // ---------------------------------------------------------------------------
 // host planning
 // ---------------------------------------------------------------------------
@@ -680,10 +752,11 @@ struct GemmPlan {
 // the split count; when CTAs would walk several units each, stream-K (mode 1)
 // removes the last round's imbalance (e.g. 1187 LM-head tiles on 148 SMs:
 // 9 units for some CTAs against 8.02 on average).
-static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k) {
+static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false) {
   GemmPlan p;
   const int sms = num_sms();
-  p.n_tiles = static_cast<int>((n + 127) / 128);
+  const int rows = glu ? 64 : 128;  // output columns per tile
+  p.n_tiles = static_cast<int>((n + rows - 1) / rows);
   p.kblocks = static_cast<int>((k + 127) / 128);
   p.bm = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
   p.m_tiles = static_cast<int>((m + p.bm - 1) / p.bm);
@@ -751,17 +824,17 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k) {
 
 static bool g_use_pdl = true;
 
-template <int BM, bool BF16>
-static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale,
-                             int sdt, void* y, int64_t ldy, int M, int N, float* ws, int* counters,
-                             const GatherArgs& g, cudaStream_t st) {
+template <int BM, bool BF16, bool GLU>
+static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tw2, const CUtensorMap& tx,
+                             const void* scale, const void* scale2, int sdt, void* y, int64_t ldy, int M, int N,
+                             float* ws, int* counters, const GatherArgs& g, cudaStream_t st) {
   using C = PCfg<BM>;
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(w8a16_persistent_kernel<BM, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(w8a16_persistent_kernel<BM, BF16, GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::SMEM);
   });
   if (int s = check_cuda(attr_err, "cudaFuncSetAttribute(w8a16_persistent_kernel)")) return s;
@@ -784,20 +857,24 @@ static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUt
   sc.kb_per_split = p.kb_per_split;
   sc.units = p.units;
   sc.work = p.work;
-  return check_cuda(cudaLaunchKernelEx(&cfg, w8a16_persistent_kernel<BM, BF16>, tw, tx, scale, sdt, y, ldy, M, N, sc,
-                                       ws, counters, g),
+  return check_cuda(cudaLaunchKernelEx(&cfg, w8a16_persistent_kernel<BM, BF16, GLU>, tw, tw2, tx, scale, scale2, sdt,
+                                       y, ldy, M, N, sc, ws, counters, g),
                     "cudaLaunchKernelEx(w8a16_persistent_kernel)");
 }
 
-template <bool BF16>
-static int dispatch_gemm(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tx, const void* scale, int sdt,
-                         void* y, int64_t ldy, int M, int N, float* ws, int* counters, const GatherArgs& g,
-                         cudaStream_t st) {
+template <bool BF16, bool GLU>
+static int dispatch_gemm(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tw2, const CUtensorMap& tx,
+                         const void* scale, const void* scale2, int sdt, void* y, int64_t ldy, int M, int N, float* ws,
+                         int* counters, const GatherArgs& g, cudaStream_t st) {
   switch (p.bm) {
-    case 16: return launch_persistent<16, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
-    case 32: return launch_persistent<32, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
-    case 64: return launch_persistent<64, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
-    default: return launch_persistent<128, BF16>(p, tw, tx, scale, sdt, y, ldy, M, N, ws, counters, g, st);
+    case 16:
+      return launch_persistent<16, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
+    case 32:
+      return launch_persistent<32, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
+    case 64:
+      return launch_persistent<64, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
+    default:
+      return launch_persistent<128, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
   }
 }
 
@@ -819,9 +896,12 @@ extern "C" size_t bw_w8a16_gemm_workspace_zeroed_bytes(int64_t m, int64_t n, int
 }
 
 namespace bw {
+// w2 / scale2 non-null: the fused gate (w, scale) / up (w2, scale2) + SwiGLU op.
 static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
                      int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace,
-                     size_t workspace_bytes, const GatherArgs& g, void* stream) {
+                     size_t workspace_bytes, const GatherArgs& g, void* stream, const int8_t* w2 = nullptr,
+                     const void* scale2 = nullptr) {
+  const bool glu = w2 != nullptr;
   if (m < 0 || n < 0 || k < 1)
     return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: need m, n >= 0 and k >= 1 (got %lld, %lld, %lld)",
                 (long long)m, (long long)n, (long long)k);
@@ -831,6 +911,8 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
     return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: unsupported scale dtype %d", scale_dtype);
   if (m == 0 || n == 0) return BW_OK;
   if (!x || !w || !scale || !y) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: null pointer");
+  if (glu && !scale2) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm_swiglu: null pointer");
+  if (glu && g.world > 0) return fail(BW_ERR_UNSUPPORTED, "int8_gemm_swiglu: no all-gather variant");
   if (ldx < k || ldw < k || ldy < n) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: row stride too small");
   if (m > (1LL << 30) || n > (1LL << 30) || k > (1LL << 30))
     return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: dimension too large");
@@ -838,10 +920,19 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = x_dtype == BW_DTYPE_BF16;
 
-  if (!tma_ok(x, ldx * 2) || !tma_ok(w, ldw)) {
+  if (!tma_ok(x, ldx * 2) || !tma_ok(w, ldw) || (glu && !tma_ok(w2, ldw))) {
     if (g.world > 0)
       return fail(BW_ERR_UNSUPPORTED, "int8_gemm (all-gather): x and w must be 16-byte aligned with 16-byte row strides");
     dim3 grid(static_cast<unsigned>((n + 127) / 128), static_cast<unsigned>(m));
+    if (glu) {
+      if (bf16)
+        w8a16_swiglu_simt_kernel<true><<<grid, 128, 0, st>>>(x, ldx, w, w2, ldw, scale, scale2, scale_dtype, y, ldy,
+                                                             (int)m, (int)n, (int)k);
+      else
+        w8a16_swiglu_simt_kernel<false><<<grid, 128, 0, st>>>(x, ldx, w, w2, ldw, scale, scale2, scale_dtype, y, ldy,
+                                                              (int)m, (int)n, (int)k);
+      return check_launch("w8a16_swiglu_simt_kernel");
+    }
     if (bf16)
       w8a16_simt_kernel<true><<<grid, 128, 0, st>>>(x, ldx, w, ldw, scale, scale_dtype, y, ldy, (int)m, (int)n, (int)k);
     else
@@ -849,7 +940,7 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
     return check_launch("w8a16_simt_kernel");
   }
 
-  const GemmPlan p = plan_gemm(m, n, k);
+  const GemmPlan p = plan_gemm(m, n, k, glu);
   if (p.units < 0) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: m=%lld n=%lld is too many output tiles",
                                (long long)m, (long long)n);
   float* ws = nullptr;
@@ -863,15 +954,31 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
     counters = static_cast<int*>(workspace);
     ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.counter_bytes);
   }
-  CUtensorMap tw, tx;
-  if (int s = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k, ldw, 128, 128,
+  CUtensorMap tw, tw2, tx;
+  if (int s = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k, ldw, glu ? 64 : 128, 128,
                            CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
+  if (glu) {
+    if (int s = make_tmap_2d(&tw2, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k, ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return s;
+  } else {
+    tw2 = tw;  // unused
+  }
   if (int s = make_tmap_2d(&tx, x, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m, k,
                            ldx * 2, p.bm, 64, CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
-  if (bf16) return dispatch_gemm<true>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, g, st);
-  return dispatch_gemm<false>(p, tw, tx, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters, g, st);
+  if (glu) {
+    if (bf16)
+      return dispatch_gemm<true, true>(p, tw, tw2, tx, scale, scale2, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
+                                       g, st);
+    return dispatch_gemm<false, true>(p, tw, tw2, tx, scale, scale2, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
+                                      g, st);
+  }
+  if (bf16)
+    return dispatch_gemm<true, false>(p, tw, tw2, tx, scale, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
+                                      g, st);
+  return dispatch_gemm<false, false>(p, tw, tw2, tx, scale, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
+                                     g, st);
 }
 }  // namespace bw
 
@@ -881,6 +988,24 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   bw::GatherArgs g = {};
   return bw::gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y, ldy, m, n, k, workspace, workspace_bytes, g,
                        stream);
+}
+
+extern "C" size_t bw_w8a16_gemm_swiglu_workspace_size(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  const bw::GemmPlan p = bw::plan_gemm(m, n, k, true);
+  return p.counter_bytes + p.partial_bytes;
+}
+
+// Fused gate/up W8A16 GEMM with the SwiGLU epilogue:
+// y = dt(silu(dt(x @ (w_gate * s_gate)^T)) * dt(x @ (w_up * s_up)^T)).
+extern "C" int bw_w8a16_gemm_swiglu(const void* x, int x_dtype, int64_t ldx, const int8_t* w_gate,
+                                    const int8_t* w_up, int64_t ldw, const void* scale_gate, const void* scale_up,
+                                    int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n, int64_t k,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  bw::GatherArgs g = {};
+  if (!w_up) return bw::fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm_swiglu: null pointer");
+  return bw::gemm_impl(x, x_dtype, ldx, w_gate, ldw, scale_gate, scale_dtype, y, ldy, m, n, k, workspace,
+                       workspace_bytes, g, stream, w_up, scale_up);
 }
 
 // Column-parallel N-split GEMM with the all-gather in the epilogue: this rank's output columns

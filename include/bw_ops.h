@@ -76,6 +76,24 @@ int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int6
                   int64_t k, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Fused gate/up W8A16 GEMM with the SwiGLU epilogue, one launch:
+ *   y[m, n] = dt( silu(g) * u ),  g = dt(x @ (w_gate * scale_gate)^T)[m, n],
+ *                                 u = dt(x @ (w_up * scale_up)^T)[m, n],  silu(g) = g / (1 + expf(-g)),
+ * i.e. swiglu(int8_gemm(x, w_gate, s_gate), int8_gemm(x, w_up, s_up)) with the silu in fp32.
+ * Replaces that composition: int8_gemm (src/blackwell_ops/kernels/int8_gemm.py:71-107) twice and
+ * swiglu (src/blackwell_ops/cuda/basic_ops.cu:112-122, cuda/__init__.py:74).
+ *   w_gate, w_up [n, k] int8 with the same row stride ldw; scale_gate, scale_up [n] scale_dtype;
+ *   x, y as for bw_w8a16_gemm.  Workspace: bw_w8a16_gemm_swiglu_workspace_size(m, n, k) bytes,
+ *   same zeroing rule as bw_w8a16_gemm (zeroed prefix: bw_w8a16_gemm_workspace_zeroed_bytes of any
+ *   split plan, 4096 bytes).
+ */
+size_t bw_w8a16_gemm_swiglu_workspace_size(int64_t m, int64_t n, int64_t k);
+int bw_w8a16_gemm_swiglu(const void* x, int x_dtype, int64_t ldx, const int8_t* w_gate, const int8_t* w_up,
+                         int64_t ldw, const void* scale_gate, const void* scale_up, int scale_dtype, void* y,
+                         int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/*
  * W8A16 GEMM that allocates nothing.  No counterpart in the reference: it exists
  * for callers that cannot provide device memory, such as a serving runtime whose
  * memory manager owns the whole GPU and refuses allocations from plug-ins, or a

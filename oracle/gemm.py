@@ -37,3 +37,17 @@ def int8_gemm(x: np.ndarray, x_dtype: str, q: np.ndarray, scale: np.ndarray, s_d
     """Oracle output in x's dtype representation: dt(fp32(acc) * fp32(scale))."""
     acc = (to_f32(x, x_dtype).astype(np.float64) @ q.astype(np.float64).T).astype(np.float32)
     return from_f32(acc * to_f32(scale, s_dtype)[None, :], x_dtype)
+
+
+def int8_gemm_swiglu(x: np.ndarray, x_dtype: str, qg: np.ndarray, sg: np.ndarray, qu: np.ndarray, su: np.ndarray,
+                     s_dtype: str) -> np.ndarray:
+    """``swiglu(int8_gemm(x, w_gate, s_gate), int8_gemm(x, w_up, s_up))`` in x's dtype representation.
+
+    The reference swiglu kernel (src/blackwell_ops/cuda/basic_ops.cu:112-122) up-casts both
+    (already dt-rounded) inputs to fp32, computes ``g / (1 + exp(-g)) * u`` in fp32 and rounds once.
+    """
+    g = to_f32(int8_gemm(x, x_dtype, qg, sg, s_dtype), x_dtype)
+    u = to_f32(int8_gemm(x, x_dtype, qu, su, s_dtype), x_dtype)
+    with np.errstate(over="ignore"):
+        silu = (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+    return from_f32((silu * u).astype(np.float32), x_dtype)
