@@ -179,23 +179,21 @@ class MergeRequantWorkload:
                            for r in self.ranks_r})
         self.flops = sum(2.0 * r * n * k for r in self.ranks_r for _, k, n in QWEN)
         self.bytes = sum(2 * n * k + 2 * r * (n + k) + n * k + 2 * n for r in self.ranks_r for _, k, n in QWEN)
-        # one batched call per (layer, adapter): all 7 projections in one launch
+        # one batched call per layer: both adapters' 7 projections (14 problems) in one launch,
+        # the two adapters of a projection side by side so the second read of the base weight
+        # follows the first (an L2 hit)
         from blackwell_ops._lib import RequantProblem
 
+        self.nprob = len(QWEN) * len(self.ranks_r)
         self.problems = []
         for li in range(layers):
-            per_r = {}
-            for r in self.ranks_r:
-                arr = (RequantProblem * len(QWEN))(*[
-                    RequantProblem(self.W[li][p].data_ptr(), k, self.A[li][r][p].data_ptr(),
-                                   self.B[li][r][p].data_ptr(), 2.0, self.Q[li][r][p].data_ptr(), k,
-                                   self.S[li][r][p].data_ptr(), n, k, r) for p, (_, k, n) in enumerate(QWEN)])
-                per_r[r] = arr
-            self.problems.append(per_r)
-        need = max(self.lib.bw_lora_merge_requant_batched_workspace_size(a, len(QWEN))
-                   for per_r in self.problems for a in per_r.values())
+            self.problems.append((RequantProblem * self.nprob)(*[
+                RequantProblem(self.W[li][p].data_ptr(), k, self.A[li][r][p].data_ptr(), self.B[li][r][p].data_ptr(),
+                               2.0, self.Q[li][r][p].data_ptr(), k, self.S[li][r][p].data_ptr(), n, k, r)
+                for p, (_, k, n) in enumerate(QWEN) for r in self.ranks_r]))
+        need = max(self.lib.bw_lora_merge_requant_batched_workspace_size(a, self.nprob) for a in self.problems)
         self.ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)  # zero before first use
-        self.launches_per_step = len(self.ranks_r)
+        self.launches_per_step = 1
 
     def config(self):
         return workload_config("cfg2", 0)
@@ -204,11 +202,10 @@ class MergeRequantWorkload:
 
     def step(self, s, st, events=None):
         li = s % self.layers
-        for r in self.ranks_r:
-            rc = self.lib.bw_lora_merge_requant_batched(self.problems[li][r], len(QWEN), self.ws.data_ptr(),
-                                                        self.ws.numel(), st)
-            if rc:
-                raise RuntimeError(self.lib.bw_last_error().decode())
+        rc = self.lib.bw_lora_merge_requant_batched(self.problems[li], self.nprob, self.ws.data_ptr(),
+                                                    self.ws.numel(), st)
+        if rc:
+            raise RuntimeError(self.lib.bw_last_error().decode())
 
     # -- end to end through the public API with host (pinned) buffers --
     def e2e_setup(self):
@@ -228,13 +225,14 @@ class MergeRequantWorkload:
         from blackwell_ops.cuda import lora_merge_requant_batched
 
         W = [t.to(self.dev, non_blocking=True) for t in self.hW]
-        for r in self.ranks_r:
-            A = [t.to(self.dev, non_blocking=True) for t in self.hA[r]]
-            B = [t.to(self.dev, non_blocking=True) for t in self.hB[r]]
-            outs = lora_merge_requant_batched(zip(W, A, B, [2.0] * len(QWEN)))
-            for p, (q, sc) in enumerate(outs):
-                self.hQ[r][p].copy_(q, non_blocking=True)
-                self.hS[r][p].copy_(sc, non_blocking=True)
+        A = {r: [t.to(self.dev, non_blocking=True) for t in self.hA[r]] for r in self.ranks_r}
+        B = {r: [t.to(self.dev, non_blocking=True) for t in self.hB[r]] for r in self.ranks_r}
+        outs = lora_merge_requant_batched([(W[p], A[r][p], B[r][p], 2.0) for p in range(len(QWEN))
+                                           for r in self.ranks_r])
+        for i, (q, sc) in enumerate(outs):
+            p, r = divmod(i, len(self.ranks_r))
+            self.hQ[self.ranks_r[r]][p].copy_(q, non_blocking=True)
+            self.hS[self.ranks_r[r]][p].copy_(sc, non_blocking=True)
 
     # -- the reference's CPU PyTorch path on a bounded sample --
     @staticmethod
