@@ -761,7 +761,10 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false) {
   p.bm = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128;
   p.m_tiles = static_cast<int>((m + p.bm - 1) / p.bm);
   const int64_t tiles = static_cast<int64_t>(p.n_tiles) * p.m_tiles;
-  const double part_cost = 2.0 * 128 * p.bm * 4;
+#ifndef BW_GEMM_PART_COST_SCALE
+#define BW_GEMM_PART_COST_SCALE 1.0
+#endif
+  const double part_cost = BW_GEMM_PART_COST_SCALE * 2.0 * 128 * p.bm * 4;
   double best = 1e300;
   int64_t best_per_cta = 1;
   for (int sp = 1; sp <= p.kblocks && sp <= 32; ++sp) {
