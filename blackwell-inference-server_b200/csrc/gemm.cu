@@ -141,7 +141,13 @@ struct PCfg {
   static constexpr int X_PANEL = BM * 128;
   static constexpr int X_BYTES = 2 * X_PANEL;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+// Ring depth: up to 8 stages.  Deeper rings (10, 11 stages of 20 KB for decode tiles) measured no
+// faster on the Llama-70B MLP decode shapes (3864 / 3805 against 3842 GB/s) and slower on 1-3 MB ones.
+#ifndef BW_GEMM_STAGE_CAP
+#define BW_GEMM_STAGE_CAP 8
+#endif
+  static constexpr int STAGES = (220 * 1024) / STAGE_BYTES > BW_GEMM_STAGE_CAP ? BW_GEMM_STAGE_CAP
+                                                                               : (220 * 1024) / STAGE_BYTES;
   static constexpr int ASTAGES = 4;  // TMEM A buffers, 64 columns each
   static constexpr int A_COL0 = 0;
   static constexpr int D_COL0 = ASTAGES * 64;

@@ -44,3 +44,28 @@ def test_host_only_entry_points():
     assert lib.bw_add_delta(None, None, -1, None) == _lib.BW_ERR_INVALID_ARGUMENT
     # empty problems are no-ops that never touch the device
     assert lib.bw_w8a16_gemm(None, 0, 8, None, 8, None, 0, None, 8, 0, 0, 8, None, 0, None) == 0
+
+
+def test_gemm_workspace_contract_host_only():
+    """Workspace planning is host-only: the zeroed counter prefix has one size (4 KB) for every
+    split shape, plans without split tiles need no workspace, stream-K plans of decode tiles keep
+    two fp32 pieces per CTA, and the fused SwiGLU op plans 64-column tiles."""
+    from blackwell_ops import _lib
+
+    lib = _lib.lib
+    shapes = [(16, 3072, 1024), (16, 1024, 3072), (16, 151936, 1024), (16, 28672, 8192), (64, 3072, 8192)]
+    for m, n, k in shapes:
+        need = lib.bw_w8a16_gemm_workspace_size(m, n, k)
+        zeroed = lib.bw_w8a16_gemm_workspace_zeroed_bytes(m, n, k)
+        assert need > 0 and zeroed == 4096 and need % 16 == 0, (m, n, k, need, zeroed)
+    # one CTA per tile with the whole K: no pieces, no counters
+    assert lib.bw_w8a16_gemm_workspace_size(2048, 14336, 4096) == 0
+    assert lib.bw_w8a16_gemm_workspace_zeroed_bytes(2048, 14336, 4096) == 0
+    # LM head at M=16: stream-K over 148 CTAs, two 128 x 16 fp32 pieces per CTA after the counters
+    sms = lib.bw_w8a16_gemm_workspace_size(16, 151936, 1024) - 4096
+    assert sms % (2 * 128 * 16 * 4) == 0 and sms // (2 * 128 * 16 * 4) >= 100
+    assert lib.bw_w8a16_gemm_swiglu_workspace_size(16, 3072, 1024) > 0
+    assert lib.bw_w8a16_gemm_swiglu_workspace_size(0, 3072, 1024) == 0
+    # argument checks of the fused op happen before any device call
+    assert lib.bw_w8a16_gemm_swiglu(None, 2, 8, None, None, 8, None, None, 0, None, 8, 1, 1, 8, None, 0,
+                                    None) == _lib.BW_ERR_INVALID_ARGUMENT
