@@ -153,16 +153,23 @@ __global__ void __launch_bounds__(512) quantize_rows_reg_kernel(const uint8_t* _
 
 // Streaming kernel for aligned rows of up to a few tens of KB: one or two CTAs
 // per SM walk rows blockIdx.x, + gridDim.x, ...; thread 0 keeps `stages` rows in
-// flight with 1-D bulk copies into a shared-memory ring.  Two groups of 128
-// threads take alternate rows (an even stage count keeps each stage with one
-// group), so two rows are reduced and quantised at once per CTA: a row's two
-// passes and block reduction are a latency chain, and one row at a time per CTA
-// measured ~1.9 TB/s of reads.  The arithmetic is the register kernel's (fp16
+// flight with 1-D bulk copies into a shared-memory ring.  Four groups of 64
+// threads take rows in turn (a stage count that is a multiple of four keeps each
+// stage with one group), so four rows are reduced and quantised at once per CTA:
+// a row's two passes and its reduction are a latency chain.  Llama-3-8B MLP bf16
+// weights: one row per CTA 2791 GB/s, two groups 3210, four groups 3470 (a ring
+// of 16 stages instead of 8 changed nothing).  The arithmetic is the register kernel's (fp16
 // rows with a normal scale use the packed quantiser, proved equal to it).
 constexpr int kQsThreads = 256;
-constexpr int kQsGroups = 2;
+#ifndef BW_QS_GROUPS
+#define BW_QS_GROUPS 4
+#endif
+#ifndef BW_QS_MAX_STAGES
+#define BW_QS_MAX_STAGES 8
+#endif
+constexpr int kQsGroups = BW_QS_GROUPS;
 constexpr int kQsGroupThreads = kQsThreads / kQsGroups;
-constexpr int kQsMaxStages = 8;
+constexpr int kQsMaxStages = BW_QS_MAX_STAGES;
 enum QuantWaitSite : int { kSiteQsFull = 301 };
 
 template <int DT>
