@@ -366,7 +366,7 @@ class QuantizeWorkload:
     One step quantises the Llama-3-8B MLP weights (14336x4096 and 4096x14336, bf16)
     of one of 4 rotating layers (940 MB > L2).  Metric GB/s."""
 
-    kernel = "quantize_rows_reg_kernel"
+    kernel = "quantize_rows_stream_kernel"
     name = "quant"
     metric_kind = "gbs"
     unit = "GB/s"
