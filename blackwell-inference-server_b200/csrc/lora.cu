@@ -223,8 +223,8 @@ constexpr int kReqGroups = 4;                      // epilogue groups of 4 warps
 constexpr int kReqSlots = 2 * kReqGroups;          // TMEM accumulator slots, 64 columns each
 constexpr int kReqTmemCols = kReqSlots * 64 <= 256 ? 256 : 512;  // allocation: a power of two
 static_assert(kReqSlots * 64 <= 512, "TMEM holds 512 columns");
-// warp 0 TMA, warp 1 MMA/TMEM, then the epilogue groups, then a second MMA warp.  Each tcgen05.mma
-// keeps its issuing thread ~120 cycles whatever N, so two issuers (alternate items) double the MMA rate.
+// warp 0 TMA, warp 1 MMA/TMEM, then the epilogue groups, then a second MMA warp: the two issuers take
+// alternate items, so one item's r/16 MMAs and commit overlap the other's (r=128 launch 41.9 -> 37.4 us).
 constexpr int kReqMmaWarp2 = 2 + 4 * kReqGroups;
 constexpr int kReqThreads = 64 + 128 * kReqGroups + 32;
 constexpr int kReqEpiThreads = 128 * kReqGroups;
