@@ -425,6 +425,87 @@ class QuantizeWorkload:
         return 2 * n * k + n * k + 2 * n, time.perf_counter() - t0, f"1024-row slice of a Llama-3-8B MLP weight (K={k})"
 
 
+class DeltaWorkload:
+    """delta / merge: LoRA delta (lora_delta) or fused merge (lora_merge) at the Llama-3-70B MLP
+    shapes (8192->28672, 28672->8192), rank r (default 128), alpha = 2r.  One step computes both
+    projections of one of 3 rotating adapters (weights 940 MB > L2).  Metric ΔW TFLOPS; the kernel
+    is HBM-bound (it writes N*K fp16), so the roofline is in GB/s."""
+
+    kernel = "lora_tc_kernel"
+    metric_kind = "tflops"
+    unit = "TFLOPS"
+
+    def __init__(self, name, dev, rank, world, r):
+        from blackwell_ops import _lib
+
+        self.lib = _lib.lib
+        self.name = name
+        self.dev = dev
+        self.r = r
+        self.xdtype = torch.float16
+        g = torch.Generator(device=dev).manual_seed(6000 + rank)
+        self.variants = 3
+        self.A = [[randn((r, k), 1.0 / math.sqrt(k), torch.float16, g, dev) for k, n in LLAMA70B_MLP]
+                  for _ in range(self.variants)]
+        self.B = [[randn((n, r), 0.01, torch.float16, g, dev) for k, n in LLAMA70B_MLP] for _ in range(self.variants)]
+        self.W = [randn((n, k), 0.02, torch.float16, g, dev) for k, n in LLAMA70B_MLP] if name == "merge" else None
+        self.D = [torch.empty((n, k), dtype=torch.float16, device=dev) for k, n in LLAMA70B_MLP]
+        self.flops = sum(2.0 * r * n * k for k, n in LLAMA70B_MLP)
+        wbytes = 4 if name == "merge" else 2
+        self.bytes = sum(wbytes * n * k + 2 * r * (n + k) for k, n in LLAMA70B_MLP)
+        self.launches_per_step = len(LLAMA70B_MLP)
+
+    def config(self):
+        return {"workload": f"{self.name}: LoRA {'delta' if self.name == 'delta' else 'delta + merge'} at the "
+                            f"Llama-3-70B MLP shapes (8192->28672, 28672->8192), r={self.r}, alpha=2r, fp16",
+                "r": self.r, "l2": "inputs larger than L2 (3 rotating adapters; the N x K fp16 output is 940 MB)",
+                "parallelism": "weak: independent replicas per rank"}
+
+    def step(self, s, st, events=None):
+        v = s % self.variants
+        for j, (k, n) in enumerate(LLAMA70B_MLP):
+            if self.name == "delta":
+                rc = self.lib.bw_lora_delta(self.A[v][j].data_ptr(), self.B[v][j].data_ptr(), self.D[j].data_ptr(),
+                                            n, k, self.r, 2.0, st)
+            else:
+                rc = self.lib.bw_lora_merge(self.W[j].data_ptr(), k, self.A[v][j].data_ptr(), self.B[v][j].data_ptr(),
+                                            2.0, self.D[j].data_ptr(), k, n, k, self.r, st)
+            if rc:
+                raise RuntimeError(self.lib.bw_last_error().decode())
+
+    def e2e_setup(self):
+        g = torch.Generator().manual_seed(11)
+        self.hA = [(torch.randn((self.r, k), generator=g) / math.sqrt(k)).half().pin_memory() for k, n in LLAMA70B_MLP]
+        self.hB = [(torch.randn((n, self.r), generator=g) * 0.01).half().pin_memory() for k, n in LLAMA70B_MLP]
+        self.hD = [torch.empty((n, k), dtype=torch.float16).pin_memory() for k, n in LLAMA70B_MLP]
+        self.h2d = sum(t.numel() * 2 for t in self.hA + self.hB)
+        self.d2h = sum(t.numel() * 2 for t in self.hD)
+
+    def e2e_step(self, s):
+        from blackwell_ops.cuda import lora_delta, lora_merge
+
+        for j in range(len(LLAMA70B_MLP)):
+            A = self.hA[j].to(self.dev, non_blocking=True)
+            B = self.hB[j].to(self.dev, non_blocking=True)
+            d = lora_delta(A, B, 2.0) if self.name == "delta" else lora_merge(self.W[j], A, B, 2.0)
+            self.hD[j].copy_(d, non_blocking=True)
+
+    def cpu_sample(self, step_index: int):
+        from oracle import torch_port
+
+        k, n = LLAMA70B_MLP[step_index % 2]
+        n = 1024  # bounded sample: a 1024-row slice of the projection
+        g = torch.Generator().manual_seed(step_index)
+        A = (torch.randn((self.r, k), generator=g) / math.sqrt(k)).half()
+        B = (torch.randn((n, self.r), generator=g) * 0.01).half()
+        W = (torch.randn((n, k), generator=g) * 0.02).half() if self.name == "merge" else None
+        t0 = time.perf_counter()
+        d = torch_port.lora_delta(A, B, 2.0)
+        if W is not None:
+            torch_port.add_delta_(W, d)
+        return 2.0 * self.r * n * k, time.perf_counter() - t0, f"1024-row slice of a 70B MLP projection (K={k})"
+
+
 class NSplitWorkload:
     """cfg5: Llama-3-70B MLP W8A16 with 32 adapter int8 copies, column-parallel over the ranks.
 
@@ -569,6 +650,8 @@ def make_workload(args, dev, rank, world):
         return GemmSweepWorkload(args.workload, dev, rank, world, m)
     if args.workload == "quant":
         return QuantizeWorkload(dev, rank, world)
+    if args.workload in ("delta", "merge"):
+        return DeltaWorkload(args.workload, dev, rank, world, args.rank)
     if args.workload == "cfg5":
         return NSplitWorkload(dev, rank, world, args.m if args.m else 16, adapters=args.adapters,
                               gather=args.gather)
@@ -595,6 +678,9 @@ def run_reference(args, rank, world):
     elif args.workload == "quant":
         sample = QuantizeWorkload.cpu_sample
         kind, unit = "gbs", "GB/s"
+    elif args.workload in ("delta", "merge"):
+        sample = lambda i: DeltaWorkload.cpu_sample(argparse.Namespace(r=args.rank, name=args.workload), i)
+        kind, unit = "tflops", "TFLOPS"
     else:
         wl_cpu = GemmCpuShim(args)
         sample, kind, unit = wl_cpu.cpu_sample, wl_cpu.metric_kind, wl_cpu.unit
@@ -671,7 +757,11 @@ def workload_config(name: str, m: int) -> dict:
 
 
 def config_for(args, wl=None):
-    return wl.config() if wl is not None else workload_config(args.workload, args.m)
+    if wl is not None:
+        return wl.config()
+    if args.workload in ("delta", "merge"):
+        return DeltaWorkload.config(argparse.Namespace(r=args.rank, name=args.workload))
+    return workload_config(args.workload, args.m)
 
 
 def main():
@@ -683,6 +773,7 @@ def main():
     ap.add_argument("--workload", default="cfg2")
     ap.add_argument("--m", type=int, default=0, help="tokens for the GEMM workloads")
     ap.add_argument("--adapters", type=int, default=32, help="cfg5: number of adapters")
+    ap.add_argument("--rank", type=int, default=128, help="delta / merge: LoRA rank r")
     ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
                     help="cfg5 on several GPUs: all-gather inside the GEMM epilogue over peer memory, or NCCL")
     ap.add_argument("--no-e2e", action="store_true")

@@ -14,6 +14,8 @@
 namespace bw {
 
 __device__ int g_status = 0;
+__device__ TraceState g_trace = {nullptr, 0u, 0u};
+__device__ long long g_wait_limit_cycles = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
 
 static thread_local char t_msg[512] = {0};
 
@@ -123,6 +125,46 @@ extern "C" const char* bw_status_string(int status) {
 extern "C" const char* bw_last_error(void) { return bw::t_msg; }
 
 extern "C" int bw_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+
+extern "C" int bw_set_wait_limit_ns(uint64_t ns) {
+  using namespace bw;
+  if (ns == 0 || ns > (1ull << 60) / 5)
+    return fail(BW_ERR_INVALID_ARGUMENT, "wait limit must be in (0, 2^60/5) ns (got %llu)", (unsigned long long)ns);
+  const long long cycles = static_cast<long long>(ns * 5 / 2);
+  return check_cuda(cudaMemcpyToSymbol(g_wait_limit_cycles, &cycles, sizeof(cycles)), "set wait limit");
+}
+
+extern "C" int bw_get_wait_limit_ns(uint64_t* ns) {
+  using namespace bw;
+  if (!ns) return fail(BW_ERR_INVALID_ARGUMENT, "null pointer");
+  long long cycles = 0;
+  if (int s = check_cuda(cudaMemcpyFromSymbol(&cycles, g_wait_limit_cycles, sizeof(cycles)), "read wait limit"))
+    return s;
+  *ns = static_cast<uint64_t>(cycles) * 2 / 5;
+  return BW_OK;
+}
+
+extern "C" int bw_trace_enable(void* buffer, size_t bytes) {
+  using namespace bw;
+  TraceState t = {nullptr, 0u, 0u};
+  if (buffer != nullptr) {
+    if (bytes < 64) return fail(BW_ERR_INVALID_ARGUMENT, "trace buffer of %zu bytes holds no record (64 bytes)", bytes);
+    if (reinterpret_cast<uintptr_t>(buffer) % 8 != 0)
+      return fail(BW_ERR_INVALID_ARGUMENT, "trace buffer must be 8-byte aligned");
+    t.buf = static_cast<unsigned long long*>(buffer);
+    t.records = static_cast<unsigned int>(bytes / 64 > 0x7FFFFFFFu ? 0x7FFFFFFFu : bytes / 64);
+  }
+  return check_cuda(cudaMemcpyToSymbol(g_trace, &t, sizeof(t)), "set trace buffer");
+}
+
+extern "C" int bw_trace_records(unsigned int* records) {
+  using namespace bw;
+  if (!records) return fail(BW_ERR_INVALID_ARGUMENT, "null pointer");
+  TraceState t;
+  if (int s = check_cuda(cudaMemcpyFromSymbol(&t, g_trace, sizeof(t)), "read trace state")) return s;
+  *records = t.next < t.records ? t.next : t.records;
+  return BW_OK;
+}
 
 extern "C" int bw_device_status(int clear, int* detail, void* stream) {
   using namespace bw;

@@ -2,7 +2,8 @@
 //
 // * PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor; every CTA loads its own tiles),
 //   and the 5th-generation tensor core (tcgen05.mma / TMEM).
-// * Bounded waits: every spin on an mbarrier gives up after BW_WAIT_LIMIT_NS,
+// * Bounded waits: every spin on an mbarrier gives up after the wait limit
+//   (default BW_WAIT_LIMIT_NS, settable per device with bw_set_wait_limit_ns),
 //   records a site id in the device status word and lets the caller unwind,
 //   so a lost arrival never hangs the GPU.
 // * Host-side status plumbing shared by all entry points.
@@ -17,17 +18,61 @@
 #include "../../include/bw_ops.h"
 
 #ifndef BW_WAIT_LIMIT_NS
-#define BW_WAIT_LIMIT_NS 4000000000ull  // 4 s: far beyond any legitimate wait
+#define BW_WAIT_LIMIT_NS 4000000000ull  // default, 4 s: far beyond any legitimate wait
 #endif
 
 namespace bw {
 
 // ---------------------------------------------------------------------------
-// device status word (first failure wins)
+// device status word (first failure wins) and the wait limit
 // ---------------------------------------------------------------------------
 extern __device__ int g_status;  // 0 = ok, else wait-site id
+// Bound of every spin wait, in SM cycles: the limit in ns x 2.5 (no SM clock is
+// above 2.5 GHz, so a wait never gives up before the limit).  Set per device by
+// bw_set_wait_limit_ns; read only once a wait has not completed at first try.
+extern __device__ long long g_wait_limit_cycles;
+__device__ __forceinline__ long long wait_limit_cycles() {
+  return *static_cast<volatile long long*>(&g_wait_limit_cycles);
+}
 
 __device__ __forceinline__ void record_timeout(int site) { atomicCAS(&g_status, 0, site); }
+
+// ---------------------------------------------------------------------------
+// device-side phase trace (off unless bw_trace_enable gave a buffer)
+//
+// Each CTA of a traced kernel claims one 64-byte record and fills it with
+// globaltimer stamps of its phases:
+//   u64 rec[8] = {gridid, blockIdx.x | gridDim.x << 32, kernel id, stamp[0..4]}
+// (stamp 0 = phase not reached).  The host groups records by gridid (one
+// launch) and reads the phases; nothing is written while tracing is off.
+// ---------------------------------------------------------------------------
+struct TraceState {
+  unsigned long long* buf;  // null: tracing off
+  unsigned int records;     // capacity
+  unsigned int next;        // next free record
+};
+extern __device__ TraceState g_trace;
+constexpr int kTraceStamps = 5;
+
+// Claim a record (call from one thread per CTA); null when tracing is off or full.
+__device__ __forceinline__ unsigned long long* trace_claim(int kernel_id) {
+  unsigned long long* buf = *static_cast<unsigned long long* volatile*>(&g_trace.buf);
+  if (buf == nullptr) return nullptr;
+  const unsigned int i = atomicAdd(&g_trace.next, 1u);
+  if (i >= g_trace.records) return nullptr;
+  unsigned long long* r = buf + static_cast<size_t>(i) * 8;
+  unsigned long long gid;
+  asm volatile("mov.u64 %0, %%gridid;" : "=l"(gid));
+  r[0] = gid;
+  r[1] = static_cast<unsigned long long>(blockIdx.x) | (static_cast<unsigned long long>(gridDim.x) << 32);
+  r[2] = static_cast<unsigned long long>(kernel_id);
+  for (int e = 0; e < kTraceStamps; ++e) r[3 + e] = 0ull;
+  return r;
+}
+__device__ __forceinline__ uint64_t globaltimer_now();
+__device__ __forceinline__ void trace_stamp(unsigned long long* rec, int e) {
+  if (rec != nullptr) rec[3 + e] = globaltimer_now();
+}
 
 // Acquire load at GPU scope (a flag another CTA publishes with a release or a fence).
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
@@ -41,6 +86,7 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+__device__ __forceinline__ uint64_t globaltimer_now() { return globaltimer(); }
 
 // ---------------------------------------------------------------------------
 // shared memory addressing
@@ -78,12 +124,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// records `site`) if it did not within BW_WAIT_LIMIT_NS (measured with the SM
+// records `site`) if it did not within the wait limit (measured with the SM
 // cycle counter, assuming at most 2.5 GHz so the bound is never shorter), or if
 // another thread of the CTA has already flagged an abort through `abort_flag`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int site) {
   if (mbar_try_wait(bar, parity)) return true;
-  const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;  // cycles
+  const long long limit = wait_limit_cycles();
   const long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -138,7 +184,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   int site) {
-  const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
+  const long long limit = wait_limit_cycles();
   const long long t0 = clock64();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;

@@ -67,7 +67,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 // Bounded wait until every word of flags[0, n) equals v; false (and the site recorded) on timeout.
 __device__ __forceinline__ bool wait_flags(const uint32_t* flags, int n, uint32_t v, int site) {
-  const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
+  const long long limit = wait_limit_cycles();
   const long long t0 = clock64();
   for (int p = 0; p < n; ++p) {
     while (ld_acquire_sys(flags + p) != v) {
@@ -146,20 +146,39 @@ struct PCfg {
 #ifndef BW_GEMM_STAGE_CAP
 #define BW_GEMM_STAGE_CAP 8
 #endif
-  static constexpr int STAGES = (220 * 1024) / STAGE_BYTES > BW_GEMM_STAGE_CAP ? BW_GEMM_STAGE_CAP
-                                                                               : (220 * 1024) / STAGE_BYTES;
-  static constexpr int ASTAGES = 4;  // TMEM A buffers, 64 columns each
+  // Decode tiles (BM < 128) give the activations a ring of their own, 80 KB deep: an x load
+  // queues behind the weight stream's in the SM's TMA unit and lands one loaded-memory latency
+  // (~6000 cycles under a full weight stream) after its issue, so it must be issued many
+  // k-blocks ahead of its MMA.  Sharing the weight ring's 8 slots made that latency pace the MMA
+  // (and through the TMEM A buffers, the dequantisers): one stage per ~900 cycles.
+  static constexpr int XSTAGES_DEC = (80 * 1024) / X_BYTES;
+  static constexpr int STAGES_DEC = (208 * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES > BW_GEMM_STAGE_CAP
+                                        ? BW_GEMM_STAGE_CAP
+                                        : (208 * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES;
+  static constexpr int STAGES_PRE = (220 * 1024) / STAGE_BYTES > BW_GEMM_STAGE_CAP ? BW_GEMM_STAGE_CAP
+                                                                                   : (220 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = BM < 128 ? STAGES_DEC : STAGES_PRE;
+  static constexpr int XSTAGES = BM < 128 ? XSTAGES_DEC : STAGES_PRE;
+// TMEM A buffers (64 columns each) between the dequantisers and the MMA: as many as the
+// accumulators leave room for, up to BW_GEMM_ASTAGES_MAX
+#ifndef BW_GEMM_ASTAGES_MAX
+#define BW_GEMM_ASTAGES_MAX 4
+#endif
+  static constexpr int NI_ = BM <= 64 ? BW_GEMM_SMALL_ISSUERS : BW_GEMM_BM128_ISSUERS;
+  static constexpr int DBUF_ = NI_ == 2 && BM == 128 ? 1 : 2;
+  static constexpr int AFIT = (512 - DBUF_ * NI_ * BM) / 64;
+  static constexpr int ASTAGES = AFIT < BW_GEMM_ASTAGES_MAX ? AFIT : BW_GEMM_ASTAGES_MAX;
   static constexpr int A_COL0 = 0;
   static constexpr int D_COL0 = ASTAGES * 64;
   static constexpr int TMEM_COLS = 512;
   // MMA issuers and accumulator buffers per issuer: BM <= 64 fits 2 x 2 x BM columns;
   // BM = 128 fits one issuer with two buffers (two issuers would leave one buffer each)
-  static constexpr int NI = BM <= 64 ? BW_GEMM_SMALL_ISSUERS : BW_GEMM_BM128_ISSUERS;
-  static constexpr int DBUF = NI == 2 && BM == 128 ? 1 : 2;
+  static constexpr int NI = NI_;
+  static constexpr int DBUF = DBUF_;
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = STAGES * W_BYTES;
-  static constexpr int OFF_BAR = OFF_X + STAGES * X_BYTES;
-  static constexpr int BAR_BYTES = 512;
+  static constexpr int OFF_BAR = OFF_X + XSTAGES * X_BYTES;
+  static constexpr int BAR_BYTES = 1024;
   static constexpr int OFF_XCH = OFF_BAR + BAR_BYTES;  // SwiGLU epilogue: 64 rows x 16 fp32 (4 KB)
   static constexpr int SMEM = OFF_XCH + 4096 + 1024;
   static constexpr int THREADS = 512;
@@ -167,7 +186,8 @@ struct PCfg {
   static_assert(NI == 1 || NI == 2, "one or two MMA issuers");
   static_assert(D_COL0 + DBUF * NI * BM <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert((4 * STAGES + 2 * ASTAGES + 4 + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
+  static_assert((2 * STAGES + 2 * XSTAGES + 2 * ASTAGES + 4 + 1) * 8 + 32 <= BAR_BYTES, "barrier area");
+  static_assert(X_PANEL % 1024 == 0 && OFF_X % 1024 == 0, "128-byte swizzled x tiles are 1024-byte aligned");
 };
 
 // The workspace starts with a counter region of the same size for every shape,
@@ -276,6 +296,7 @@ __global__ void __launch_bounds__(512, 1)
                             const GatherArgs g) {
   using C = PCfg<BM>;
   constexpr int STAGES = C::STAGES;
+  constexpr int XSTAGES = C::XSTAGES;
   constexpr int ASTAGES = C::ASTAGES;
   constexpr int NI = C::NI;
   constexpr int DBUF = C::DBUF;
@@ -290,20 +311,24 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* dfull = aempty + ASTAGES;    // 2
   uint64_t* dempty = dfull + 2;          // 2
   uint64_t* final_bar = dempty + 2;      // 1
-  uint64_t* xfull = final_bar + 1;       // STAGES: the x tiles of a stage (full[] covers its W tile)
-  uint64_t* xempty = xfull + STAGES;     // STAGES: the MMAs that read a stage's x tiles are done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + STAGES);
+  uint64_t* xfull = final_bar + 1;       // XSTAGES: the x tiles of a k-block (full[] covers its W tile)
+  uint64_t* xempty = xfull + XSTAGES;    // XSTAGES: the MMAs that read a k-block's x tiles are done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + XSTAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket = abort_flag + 1;
+  unsigned long long** trace_slot = reinterpret_cast<unsigned long long**>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    *trace_slot = trace_claim(GLU ? 2 : 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&xfull[s], 1);
       mbar_init(&empty[s], 4);       // W tile read into registers by one group of 4 dequantiser warps
+    }
+    for (int s = 0; s < XSTAGES; ++s) {
+      mbar_init(&xfull[s], 1);
       mbar_init(&xempty[s], NI);     // x tiles: a commit per issuer
     }
     for (int t = 0; t < ASTAGES; ++t) {
@@ -331,7 +356,11 @@ __global__ void __launch_bounds__(512, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) pdl_launch_dependents();
+  unsigned long long* const trec = *trace_slot;
+  if (threadIdx.x == 0) {
+    trace_stamp(trec, 0);
+    pdl_launch_dependents();
+  }
 
   if (warp == 0) {
     // ---------------- TMA producer: weight tiles ----------------
@@ -377,9 +406,9 @@ __global__ void __launch_bounds__(512, 1)
       while (ok && wk.next(sc, sg)) {
         const int mt = sg.t % sc.m_tiles;
         for (int i = 0; i < sg.nkb; ++i, ++it) {
-          const int s = it % STAGES;
+          const int s = it % XSTAGES;
           const int kx = (sg.k0 + i) * C::BK;
-          if (it >= STAGES && !mbar_wait(&xempty[s], ((it / STAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
+          if (it >= XSTAGES && !mbar_wait(&xempty[s], ((it / XSTAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
             ok = false;
             break;
           }
@@ -389,8 +418,8 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
       if (!ok)
-        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
-          mbar_wait(&xfull[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
+        for (int j = (it > XSTAGES ? it - XSTAGES : 0); j < it; ++j)
+          mbar_wait(&xfull[j % XSTAGES], (j / XSTAGES) & 1, nullptr, kSitePDrain);
     }
   } else if (warp == 1 || (NI == 2 && warp == 14)) {
     // ---------------- MMA issuers ----------------
@@ -408,8 +437,8 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem + C::D_COL0 + (b * NI + h) * BM;
         for (int i = 0; i < sg.nkb; ++i, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
+          const int s = it % XSTAGES;
+          const uint32_t ph = (it / XSTAGES) & 1;
           const int t = it % ASTAGES;
           const uint32_t pa = (it / ASTAGES) & 1;
           if (!mbar_wait(&afull[t], pa, abort_flag, kSitePMmaA) || !mbar_wait(&xfull[s], ph, abort_flag, kSitePMmaFull)) {
@@ -432,6 +461,7 @@ __global__ void __launch_bounds__(512, 1)
       // every issued MMA has completed before TMEM is released
       umma_commit(final_bar);
       mbar_wait(final_bar, 0, nullptr, kSitePFinal);
+      if (h == 0) trace_stamp(trec, 2);
     }
   } else if (warp < 10) {
     // ---------------- dequantisers ----------------
@@ -457,6 +487,7 @@ __global__ void __launch_bounds__(512, 1)
           ok = false;
           break;
         }
+        if (it == 0 && threadIdx.x == 64) trace_stamp(trec, 1);
         const uint8_t* src = sW + s * C::W_BYTES + row * 128;
         uint32_t out[2][32];
 #pragma unroll
@@ -672,6 +703,7 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
     }
+    if (warp == 10 && lane == 0) trace_stamp(trec, 3);
     if (g.world > 0) {
       // done handshake: the last CTA of this rank tells every peer that this rank's columns
       // are in its Y, then waits until every peer has said the same (bounded)
@@ -687,6 +719,7 @@ __global__ void __launch_bounds__(512, 1)
           wait_flags(mine + g.world, g.world, epoch, kSiteGDone);
           atomicExch(mine + 2 * g.world, 0u);  // the CTA ticket, for the next call
           st_release_sys(mine + 2 * g.world + 1, epoch);
+          trace_stamp(trec, 4);
         }
       }
     }

@@ -521,7 +521,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
             atomicAdd(&gsync[1], 1);   // open the waiters first
             atomicExch(&gsync[0], 0);  // the count is next needed by the next call
           } else {
-            const long long limit = static_cast<long long>(BW_WAIT_LIMIT_NS) * 5 / 2;
+            const long long limit = wait_limit_cycles();
             const long long t0 = clock64();
             while (ld_acquire_gpu(&gsync[1]) == gen) {
               if (clock64() - t0 > limit) {

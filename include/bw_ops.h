@@ -205,6 +205,32 @@ int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int c
  */
 int bw_device_status(int clear, int* detail, void* stream);
 
+/*
+ * Bound of every spin wait inside this library's kernels (mbarrier waits, the
+ * all-gather's peer-flag waits, the requantiser's grid barrier), for the
+ * current device, in nanoseconds (default 4 s).  A wait that runs out records
+ * its site in the device status (bw_device_status) and its kernel unwinds
+ * without writing the rest of its output.  No reference counterpart: the
+ * reference's kernels have no spin waits.  Takes effect for kernels launched
+ * after the call; not to be changed while kernels of this library run.
+ */
+int bw_set_wait_limit_ns(uint64_t ns);
+int bw_get_wait_limit_ns(uint64_t* ns);
+
+/*
+ * Device-side phase trace for the current device (no reference counterpart;
+ * the reference profiles with torch.profiler).  While a buffer is set, each
+ * CTA of a traced kernel (the W8A16 GEMM family) claims one 64-byte record
+ *   u64 {gridid, blockIdx | gridDim << 32, kernel id, t[0..4]}
+ * with globaltimer stamps (ns; 0 = phase not reached): t0 CTA start, t1 first
+ * weight tile in shared memory, t2 last MMA complete, t3 epilogue done, t4
+ * all-gather completion handshake done (the CTA that ran it).  buffer = NULL
+ * turns tracing off; bw_trace_records gives the records written so far
+ * (records past the buffer's capacity are dropped).
+ */
+int bw_trace_enable(void* buffer, size_t bytes);
+int bw_trace_records(unsigned int* records);
+
 #ifdef __cplusplus
 }
 #endif

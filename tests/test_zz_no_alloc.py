@@ -3,17 +3,30 @@
 Some callers cannot give the library device memory (a serving runtime whose
 memory manager owns the whole GPU, a foreign-language binding with no CUDA
 allocator), so this entry point keeps its split-K scratch in a fixed array
-inside libbw_ops.so.  This test calls it through the C ABI and checks, on two
-calls in a row, that it returns what the workspace-taking bw_w8a16_gemm
-returns, within the GEMM tests' tolerance (max |err| <= 1e-2, relative
-<= 1e-3), and that shapes needing more scratch than the array are refused.
-It lives in its own file, collected last, and needs nothing from other tests.
+inside libbw_ops.so.  This test calls it through the C ABI, on two calls in a
+row, for shapes whose plan does use that scratch, and checks that
+
+* it returns exactly the bits of the workspace-taking bw_w8a16_gemm (the
+  kernel, its plan and its k-ordered reduction are the same, so the result is
+  deterministic), and
+* it meets the GEMM tolerance against the fp32 oracle (max |err| <= 1e-2,
+  relative <= 1e-3 against the float64-accumulated dequantise-then-matmul),
+
+and that shapes needing more scratch than the array are refused.  It lives in
+its own file, collected last, and needs nothing from other tests.
 """
+import numpy as np
 import pytest
+
+from oracle import gemm, inputs, quant
+from oracle.numerics import F16
 
 pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
+
+# every shape here plans split-K or stream-K pieces, i.e. needs scratch
+SHAPES = [(16, 1024, 4096), (1, 3072, 1024), (48, 2048, 2048), (64, 3584, 8192), (16, 151936, 1024)]
 
 
 def _gemm_with_workspace(lib, st, x, q, s, m, n, k):
@@ -26,30 +39,34 @@ def _gemm_with_workspace(lib, st, x, q, s, m, n, k):
     return y, need
 
 
-@pytest.mark.parametrize("m,n,k", [(16, 1024, 4096), (1, 3072, 1024), (48, 2048, 2048), (200, 256, 1024),
-                                   (16, 151936, 1024)])
-def test_noalloc_matches_workspace_entry_point(m, n, k):
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_noalloc_matches_workspace_entry_point_and_oracle(m, n, k):
     from blackwell_ops import _lib
 
     lib = _lib.lib
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
     st = _lib.stream_ptr(dev)
-    g = torch.Generator(device=dev).manual_seed(m * 7 + n + k)
-    x = torch.randn(m, k, generator=g, device=dev).half()
-    q = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
-    s = (torch.rand(n, generator=g, device=dev) * 1e-3 + 1e-4).half()
+    w = inputs.weight(m * 7 + n + k, n, k, F16)
+    qn, sn = quant.quantize_weight_int8(w, F16)
+    xn = inputs.activations(m + k, m, k, F16)
+    x = torch.from_numpy(xn).to(dev)
+    q = torch.from_numpy(qn).to(dev)
+    s = torch.from_numpy(sn).to(dev)
     ref, need = _gemm_with_workspace(lib, st, x, q, s, m, n, k)
-    assert need <= lib.bw_w8a16_gemm_static_scratch_bytes()
+    assert 0 < need <= lib.bw_w8a16_gemm_static_scratch_bytes(), need
+    want = gemm.exact(xn, F16, qn, sn, F16)
     for _ in range(2):
         y = torch.full((m, n), float("nan"), dtype=torch.float16, device=dev)
         rc = lib.bw_w8a16_gemm_noalloc(x.data_ptr(), 0, k, q.data_ptr(), k, s.data_ptr(), 0, y.data_ptr(), n, m, n,
                                        k, st)
         assert rc == 0, lib.bw_last_error()
         torch.cuda.synchronize()
-        err = (y.double() - ref.double()).abs()
-        assert float(err.max()) <= 1e-2
-        assert float(err.norm() / ref.double().norm()) <= 1e-3
+        assert torch.equal(y.view(torch.int16), ref.view(torch.int16)), "differs from bw_w8a16_gemm"
+        got = y.float().cpu().numpy().astype(np.float64)
+        err = np.abs(got - want)
+        assert err.max() <= 1e-2, err.max()
+        assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-3
     assert _lib.device_status() == 0
 
 
