@@ -1,11 +1,19 @@
 """Benchmark harness (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg2|cfg1|cfg3|cfg4|cfg5] [--m M]
+                    [--workload cfg5|cfg1|cfg2|cfg3|cfg4|quant|delta|merge] [--m M]
 
 Workloads (synthetic seeded data, weights random-init):
 
-  cfg2 (default; configs[1])  LoRA delta -> merge -> per-channel int8 requantisation
+  cfg5 (default)  Llama-3-70B MLP W8A16 decode (8192->28672, 28672->8192), M=16 tokens,
+        bf16, with 32 adapter int8 copies (merged and requantised at set-up, not
+        timed); a step serves one adapter (round robin, 470 MB of int8 weights per
+        step > L2).  Column-parallel N-split over the N GPUs: each rank streams its
+        1/N of the rows and the output slices are all-gathered inside the GEMM
+        epilogue over NVLink peer memory (--gather fused, default) or by NCCL
+        (--gather nccl).  Strong scaling.  Metric: GB/s of the whole job (the
+        metric's lead quantity, W8A16 decode GEMM vs HBM).
+  cfg2  LoRA delta -> merge -> per-channel int8 requantisation
         at the Qwen3-0.6B layer shapes: 7 projections x r in {16, 128}, alpha = 2r
         (scaling 2).  One step merges one decoder layer's 7 projections for both
         adapters; successive steps walk 28 distinct layers (412 MB of fp16
@@ -19,9 +27,14 @@ Workloads (synthetic seeded data, weights random-init):
         + LM head 1024->151936, M tokens (default 16).  Metric GB/s.
   cfg4  prefill W8A16 at Llama-3-8B MLP shapes (4096->14336, 14336->4096), bf16,
         M tokens (default 2048).  Metric TFLOPS.
-  cfg5  Llama-3-70B MLP W8A16 with 32 adapter int8 copies, column-parallel N-split
-        over the N GPUs with an NCCL all-gather of the output slices, M tokens
-        (default 16).  Metric GB/s (decode) or TFLOPS (M >= 512).
+  quant  quantize_weight_int8 of the Llama-3-8B MLP weights (bf16), GB/s.
+  delta / merge  lora_delta / lora_merge at the Llama-3-70B MLP shapes, r = --rank
+        (default 128), ΔW TFLOPS with the roofline in GB/s.
+
+--trace adds "phases": device-side globaltimer stamps of a few replayed steps
+(per GEMM launch: CTA start spread, first weight tile landed, last MMA done,
+epilogue done, all-gather handshake done, gap to the next launch), so the JSON
+line names the phase that bounds a step.
 
 Timing: W untimed warm-up steps, then exactly K steps between a barrier +
 synchronize on both sides, CUDA events on the launching stream, max over ranks.
@@ -658,6 +671,29 @@ def make_workload(args, dev, rank, world):
     raise SystemExit(f"unknown workload {args.workload}")
 
 
+def summarize_phases(launches, per_step: int) -> dict:
+    """Median over the traced steps of each GEMM launch's phase ends (us from its first CTA
+    start) and of the gap from one launch's last phase to the next launch's first CTA start."""
+    import statistics
+
+    rows = [l.phases_us() for l in launches]
+    ends = []
+    for l in launches:
+        st = l.stamps.double()
+        ends.append((float(st[:, 0][st[:, 0] > 0].min()), float(st.max())))
+    out = {"launches_traced": len(rows), "per_launch_us": {}}
+    keys = sorted({k for r in rows for k in r})
+    for k in keys:
+        vals = [r[k] for r in rows if k in r]
+        out["per_launch_us"][k] = round(statistics.median(vals), 3)
+    gaps = [(ends[i + 1][0] - ends[i][1]) / 1e3 for i in range(len(ends) - 1)]
+    if gaps:
+        out["gap_between_launches_us"] = round(statistics.median(gaps), 3)
+    durs = [(e - b) / 1e3 for b, e in ends]
+    out["launch_span_us"] = round(statistics.median(durs), 3)
+    return out
+
+
 def amount_of(wl) -> float:
     return wl.flops if wl.metric_kind == "tflops" else wl.bytes
 
@@ -770,7 +806,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", default="cfg2")
+    ap.add_argument("--workload", default="cfg5")
+    ap.add_argument("--trace", action="store_true", help="add device-side phase stamps of a few steps")
     ap.add_argument("--m", type=int, default=0, help="tokens for the GEMM workloads")
     ap.add_argument("--adapters", type=int, default=32, help="cfg5: number of adapters")
     ap.add_argument("--rank", type=int, default=128, help="delta / merge: LoRA rank r")
@@ -885,6 +922,16 @@ def main():
     if wl.metric_kind == "tflops" and roof["bound"] == "hbm":
         roof["tensor_tflops"] = round(achieved_tf, 2)
 
+    # ---- device-side phase stamps of a few replayed steps (--trace) ----
+    phases = None
+    if args.trace:
+        from blackwell_ops.device import Trace
+
+        with Trace(records=4096, device=dev) as tr:
+            for s in range(4):
+                replay(s)
+        phases = summarize_phases(tr.launches(), wl.launches_per_step)
+
     # ---- end to end through the public API, host buffers ----
     e2e = None
     if not args.no_e2e:
@@ -935,17 +982,22 @@ def main():
                 "data": "synthetic (seeded), random-init weights", "config": wl.config(), "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": wl.launches_per_step * args.steps,
                 "clocks": sampler.summary(), "device_status": status}
+        if phases is not None:
+            line["phases"] = phases
         print(json.dumps(line), flush=True)
     if world > 1:
         # the result is out; bound the teardown so a stuck communicator cannot hold the GPUs
         import threading
 
-        def _bail():
+        def _bail_timeout():
+            # the JSON line is out, but a teardown that does not finish is a failure of the run
             sys.stdout.flush()
+            sys.stderr.write(f"rank {rank}: teardown timeout (barrier / destroy_process_group did not finish "
+                             f"within 60 s)\n")
             sys.stderr.flush()
-            os._exit(0)
+            os._exit(3)
 
-        guard = threading.Timer(60.0, _bail)
+        guard = threading.Timer(60.0, _bail_timeout)
         guard.daemon = True
         guard.start()
         barrier()

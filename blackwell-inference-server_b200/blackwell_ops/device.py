@@ -103,6 +103,9 @@ class Launch:
             col = s[:, i][s[:, i] > 0]
             if col.numel():
                 out[name] = round((float(col.max()) - t0) / 1e3, 3)
+                if name == "mma_done":  # spread of the CTAs' mainloop ends (load balance)
+                    out["mma_done_first"] = round((float(col.min()) - t0) / 1e3, 3)
+                    out["mma_done_median"] = round((float(col.median()) - t0) / 1e3, 3)
         return out
 
 

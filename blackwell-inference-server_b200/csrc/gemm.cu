@@ -125,14 +125,20 @@ __device__ __forceinline__ float round_out(float v) {
 // preceding kernel (weights do not depend on it); the activation producer and
 // the epilogue wait (griddepcontrol.wait) before their first global access.
 // ---------------------------------------------------------------------------
-#ifndef BW_GEMM_SMALL_ISSUERS
-#define BW_GEMM_SMALL_ISSUERS 2
-#endif
 #ifndef BW_GEMM_STREAMK
 #define BW_GEMM_STREAMK 1
 #endif
-#ifndef BW_GEMM_BM128_ISSUERS
-#define BW_GEMM_BM128_ISSUERS 1
+// MMA issuer threads.  A thread issuing tcgen05.mma (M=128, N=16, K=16, A from TMEM slices that
+// change every k-block) completes one per ~81 cycles however many accumulators it uses, plus
+// ~120 cycles per tcgen05.commit; the tensor pipe overlaps the MMAs of different issuer threads
+// (microbenchmark, 148 CTAs: 1, 2, 3, 4 issuers -> 81, 40, 27, 20 cycles per MMA aggregate).  A
+// 16 KB k-block is eight MMAs, so one issuer caps a CTA near 2.5 TB/s-equivalent of weights.
+// Decode tiles (BM <= 64) run two issuers (warps 1, 14), each taking every other k-block into
+// its own accumulator; BM = 128 one.  A third issuer (warp 15, with the weight producer also
+// loading the activation tiles) measured slower on the Llama-3-70B MLP decode shapes (3.1 against
+// 4.0 TB/s): the single producer then issued one weight tile per ~1250 cycles.
+#ifndef BW_GEMM_DEC_ISSUERS
+#define BW_GEMM_DEC_ISSUERS 2
 #endif
 template <int BM>
 struct PCfg {
@@ -141,40 +147,31 @@ struct PCfg {
   static constexpr int X_PANEL = BM * 128;
   static constexpr int X_BYTES = 2 * X_PANEL;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-// Ring depth: up to 8 stages.  Deeper rings (10, 11 stages of 20 KB for decode tiles) measured no
-// faster on the Llama-70B MLP decode shapes (3864 / 3805 against 3842 GB/s) and slower on 1-3 MB ones.
-#ifndef BW_GEMM_STAGE_CAP
-#define BW_GEMM_STAGE_CAP 8
-#endif
-  // Decode tiles (BM < 128) give the activations a ring of their own, 80 KB deep: an x load
-  // queues behind the weight stream's in the SM's TMA unit and lands one loaded-memory latency
-  // (~6000 cycles under a full weight stream) after its issue, so it must be issued many
-  // k-blocks ahead of its MMA.  Sharing the weight ring's 8 slots made that latency pace the MMA
-  // (and through the TMEM A buffers, the dequantisers): one stage per ~900 cycles.
-  static constexpr int XSTAGES_DEC = (80 * 1024) / X_BYTES;
-  static constexpr int STAGES_DEC = (208 * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES > BW_GEMM_STAGE_CAP
-                                        ? BW_GEMM_STAGE_CAP
-                                        : (208 * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES;
-  static constexpr int STAGES_PRE = (220 * 1024) / STAGE_BYTES > BW_GEMM_STAGE_CAP ? BW_GEMM_STAGE_CAP
-                                                                                   : (220 * 1024) / STAGE_BYTES;
+  static constexpr int NI = BM <= 32 ? BW_GEMM_DEC_ISSUERS : BM == 64 ? 2 : 1;
+  // the producer of the weight tiles also loads the activation tiles (else warp 15 does)
+  static constexpr bool ONE_PRODUCER = NI >= 3;
+  // Prefill ring: weight + activation tiles per stage, up to 4 stages of 48 KB.
+  static constexpr int STAGES_PRE = (220 * 1024) / STAGE_BYTES > 8 ? 8 : (220 * 1024) / STAGE_BYTES;
+  // Decode rings.  The weight stream is bound by the bytes a CTA keeps in flight (Little's law:
+  // under a full stream a 16 KB tile lands ~3-5 us after its TMA issue; probes streaming the same
+  // boxes reach ~6 TB/s with 8 x 16 KB in flight per SM when slots are released at once), so the
+  // weight ring takes most of shared memory.  The activations get their own ring, deeper than the
+  // weight ring by the k-blocks the MMAs may lag the dequantisers: a TMA load queues behind the
+  // weight tiles already issued, so an activation tile must be issued with (or before) its
+  // k-block's weight tile; with a shallow ring its slot frees only when an MMA completes, and the
+  // tile then landed a full loaded latency after the MMA was due (one stage per ~900 cycles).
+  static constexpr int XSTAGES_DEC = BM == 16 ? 16 : BM == 32 ? 12 : 5;
+  static constexpr int STAGES_DEC = (208 * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES;
   static constexpr int STAGES = BM < 128 ? STAGES_DEC : STAGES_PRE;
   static constexpr int XSTAGES = BM < 128 ? XSTAGES_DEC : STAGES_PRE;
-// TMEM A buffers (64 columns each) between the dequantisers and the MMA: as many as the
-// accumulators leave room for, up to BW_GEMM_ASTAGES_MAX
-#ifndef BW_GEMM_ASTAGES_MAX
-#define BW_GEMM_ASTAGES_MAX 4
-#endif
-  static constexpr int NI_ = BM <= 64 ? BW_GEMM_SMALL_ISSUERS : BW_GEMM_BM128_ISSUERS;
-  static constexpr int DBUF_ = NI_ == 2 && BM == 128 ? 1 : 2;
-  static constexpr int AFIT = (512 - DBUF_ * NI_ * BM) / 64;
-  static constexpr int ASTAGES = AFIT < BW_GEMM_ASTAGES_MAX ? AFIT : BW_GEMM_ASTAGES_MAX;
+  // TMEM: A buffers (64 columns each) between the dequantisers and the MMAs, as many as the
+  // double-buffered accumulators (DBUF x NI x BM columns) leave room for, up to 6.
+  static constexpr int DBUF = 2;
+  static constexpr int AFIT = (512 - DBUF * NI * BM) / 64;
+  static constexpr int ASTAGES = AFIT < 6 ? AFIT : 6;
   static constexpr int A_COL0 = 0;
   static constexpr int D_COL0 = ASTAGES * 64;
   static constexpr int TMEM_COLS = 512;
-  // MMA issuers and accumulator buffers per issuer: BM <= 64 fits 2 x 2 x BM columns;
-  // BM = 128 fits one issuer with two buffers (two issuers would leave one buffer each)
-  static constexpr int NI = NI_;
-  static constexpr int DBUF = DBUF_;
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = STAGES * W_BYTES;
   static constexpr int OFF_BAR = OFF_X + XSTAGES * X_BYTES;
@@ -183,9 +180,11 @@ struct PCfg {
   static constexpr int SMEM = OFF_XCH + 4096 + 1024;
   static constexpr int THREADS = 512;
   static_assert(BM >= 16 && BM <= 128 && BM % 16 == 0, "UMMA N for M=128");
-  static_assert(NI == 1 || NI == 2, "one or two MMA issuers");
+  static_assert(NI >= 1 && NI <= 3, "one to three MMA issuers");
+  static_assert(ASTAGES >= 2, "TMEM A buffers");
   static_assert(D_COL0 + DBUF * NI * BM <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(!ONE_PRODUCER || XSTAGES >= STAGES + ASTAGES, "activation ring must not stall the producer");
   static_assert((2 * STAGES + 2 * XSTAGES + 2 * ASTAGES + 4 + 1) * 8 + 32 <= BAR_BYTES, "barrier area");
   static_assert(X_PANEL % 1024 == 0 && OFF_X % 1024 == 0, "128-byte swizzled x tiles are 1024-byte aligned");
 };
@@ -329,11 +328,11 @@ __global__ void __launch_bounds__(512, 1)
     }
     for (int s = 0; s < XSTAGES; ++s) {
       mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], NI);     // x tiles: a commit per issuer
+      mbar_init(&xempty[s], 1);      // x tiles: a commit by the k-block's issuer
     }
     for (int t = 0; t < ASTAGES; ++t) {
       mbar_init(&afull[t], 4);
-      mbar_init(&aempty[t], NI);
+      mbar_init(&aempty[t], 1);
     }
     for (int b = 0; b < DBUF; ++b) {
       mbar_init(&dfull[b], NI);
@@ -363,16 +362,39 @@ __global__ void __launch_bounds__(512, 1)
   }
 
   if (warp == 0) {
-    // ---------------- TMA producer: weight tiles ----------------
-    // Weights do not depend on the preceding kernel (no griddepcontrol.wait here), and a
-    // slot is free as soon as a dequantiser group has read it into registers.
+    // ---------------- TMA producer: weight tiles (and, with ONE_PRODUCER, activation tiles) ----------------
+    // Weights do not depend on the preceding kernel: the first ring of weight tiles is issued
+    // before griddepcontrol.wait, and a slot is free as soon as a dequantiser group has read it
+    // into registers.  Activation tiles follow their k-block's weight tile in the TMA queue.
     if (lane == 0) {
       // a weight tile used by several M-tiles stays in L2 for the CTAs that share it
       const uint64_t pol_w = sc.m_tiles > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
-      int it = 0;
-      bool ok = true;
-      SegWalk wk(sc, blockIdx.x, gridDim.x);
-      Seg sg;
+      const uint64_t pol_x = l2_policy_evict_last();
+      int it = 0, jx = 0, ix = 0;
+      bool ok = true, waited = !C::ONE_PRODUCER, xseg = false;
+      SegWalk wk(sc, blockIdx.x, gridDim.x), wx(sc, blockIdx.x, gridDim.x);
+      Seg sg, sx;
+      // activation tiles of k-blocks [jx, upto)
+      auto load_x_until = [&](int upto) {
+        while (ok && jx < upto) {
+          if (!xseg || ix >= sx.nkb) {
+            xseg = wx.next(sc, sx);
+            ix = 0;
+            if (!xseg) return;
+          }
+          const int xs = jx % XSTAGES;
+          if (jx >= XSTAGES && !mbar_wait(&xempty[xs], ((jx / XSTAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
+            ok = false;
+            return;
+          }
+          const int kx = (sx.k0 + ix) * C::BK, m0 = (sx.t % sc.m_tiles) * BM;
+          mbar_arrive_expect_tx(&xfull[xs], C::X_BYTES);
+          tma_load_2d(sX + xs * C::X_BYTES, &tm_x, &xfull[xs], kx, m0, pol_x);
+          tma_load_2d(sX + xs * C::X_BYTES + C::X_PANEL, &tm_x, &xfull[xs], kx + 64, m0, pol_x);
+          ++ix;
+          ++jx;
+        }
+      };
       while (ok && wk.next(sc, sg)) {
         const int nt = sg.t / sc.m_tiles;
         for (int i = 0; i < sg.nkb; ++i, ++it) {
@@ -388,13 +410,31 @@ __global__ void __launch_bounds__(512, 1)
           } else {
             tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 128, pol_w);
           }
+          if constexpr (C::ONE_PRODUCER) {
+            if (!waited && it + 1 >= STAGES) {
+              pdl_wait();
+              waited = true;
+            }
+            if (waited) load_x_until(it + 1);
+          }
         }
       }
-      if (!ok)  // wait (bounded) for the copies still in flight into this CTA's shared memory
+      if constexpr (C::ONE_PRODUCER) {
+        if (ok && !waited) {  // fewer k-blocks than ring slots
+          pdl_wait();
+          waited = true;
+        }
+        load_x_until(it);
+      }
+      if (!ok) {  // wait (bounded) for the copies still in flight into this CTA's shared memory
         for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
           mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
+        if constexpr (C::ONE_PRODUCER)
+          for (int j = (jx > XSTAGES ? jx - XSTAGES : 0); j < jx; ++j)
+            mbar_wait(&xfull[j % XSTAGES], (j / XSTAGES) & 1, nullptr, kSitePDrain);
+      }
     }
-  } else if (warp == 15) {
+  } else if (warp == 15 && !C::ONE_PRODUCER) {
     // ---------------- TMA producer: activation tiles (after the predecessor) ----------------
     if (lane == 0) {
       const uint64_t pol_x = l2_policy_evict_last();
@@ -421,12 +461,14 @@ __global__ void __launch_bounds__(512, 1)
         for (int j = (it > XSTAGES ? it - XSTAGES : 0); j < it; ++j)
           mbar_wait(&xfull[j % XSTAGES], (j / XSTAGES) & 1, nullptr, kSitePDrain);
     }
-  } else if (warp == 1 || (NI == 2 && warp == 14)) {
+  } else if (warp == 1 || (NI >= 2 && warp == 14) || (NI >= 3 && warp == 15)) {
     // ---------------- MMA issuers ----------------
     if (lane == 0) {
+      // Issuer h takes the k-blocks it with it % NI == h, all eight K=16 slices of each, into
+      // its own accumulator, so the issuers' MMA streams, waits and commits run side by side.
+      // The epilogue adds the accumulators in a fixed order.
       constexpr uint32_t idesc = make_idesc_f16(128, BM, BF16, false);
-      constexpr int KK = 8 / NI;        // K=16 slices per k-block for each issuer
-      const int h = warp == 1 ? 0 : 1;  // issuer index
+      const int h = warp == 1 ? 0 : warp == 14 ? 1 : 2;  // issuer index
       int it = 0, j = 0;
       bool ok = true;
       SegWalk wk(sc, blockIdx.x, gridDim.x);
@@ -436,7 +478,9 @@ __global__ void __launch_bounds__(512, 1)
         if (!mbar_wait(&dempty[b], ((j / DBUF) & 1) ^ 1, abort_flag, kSitePMmaD)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + C::D_COL0 + (b * NI + h) * BM;
+        uint32_t acc = 0;  // 0 until this issuer's first MMA of the segment
         for (int i = 0; i < sg.nkb; ++i, ++it) {
+          if (NI > 1 && it % NI != h) continue;
           const int s = it % XSTAGES;
           const uint32_t ph = (it / XSTAGES) & 1;
           const int t = it % ASTAGES;
@@ -448,10 +492,10 @@ __global__ void __launch_bounds__(512, 1)
           tc_fence_after();
           const uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
 #pragma unroll
-          for (int k2 = 0; k2 < KK; ++k2) {
-            const int kk = h * KK + k2;
+          for (int kk = 0; kk < 8; ++kk) {
             const uint64_t bd = make_sdesc(x_base + (kk >> 2) * C::X_PANEL + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-            umma_f16_ts(d_tmem, tmem + C::A_COL0 + t * 64 + kk * 8, bd, idesc, (i | k2) != 0 ? 1u : 0u);
+            umma_f16_ts(d_tmem, tmem + C::A_COL0 + t * 64 + kk * 8, bd, idesc, acc);
+            acc = 1u;
           }
           umma_commit(&xempty[s]);
           umma_commit(&aempty[t]);
@@ -547,12 +591,15 @@ __global__ void __launch_bounds__(512, 1)
       gather_ok = !named_bar_any(1, 128, !gather_ok);
     }
     int j = 0;
+    int it0 = 0;  // this CTA's k-block count before the segment
     SegWalk wk(sc, blockIdx.x, gridDim.x);
     Seg sg;
-    for (; wk.next(sc, sg); ++j) {
+    for (; wk.next(sc, sg); it0 += sg.nkb, ++j) {
       const int t = sg.t;
       const int nt = t / sc.m_tiles;
       const int mt = t - nt * sc.m_tiles;
+      // issuer h holds part of this segment iff one of its k-blocks (it % NI == h) lies in it
+      auto has = [&](int h) { return sg.nkb >= NI || (h - it0 % NI + NI) % NI < sg.nkb; };
       const int n = GLU ? nt * 64 + (row & 63) : nt * 128 + row;
       const int m0 = mt * BM;
       const void* srow = GLU && row >= 64 ? scale2 : scale;
@@ -561,20 +608,19 @@ __global__ void __launch_bounds__(512, 1)
       if (named_bar_any(1, 128, !ok || *abort_flag)) break;  // same decision in all 4 warps
       tc_fence_after();
       const uint32_t taddr = lane_addr + b * NI * BM;
-      // 16 accumulator columns of this thread's row: issuer 0's sum plus issuer 1's
+      // 16 accumulator columns of this thread's row: the sum over the issuers that took part
+      // of the segment, in issuer order (a fixed order, so results do not depend on timing)
       auto load_acc = [&](int c0, float (&v)[16]) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c0, r);
-        if constexpr (NI == 2) {
-          uint32_t r1[16];
-          tmem_ld16(taddr + BM + c0, r1);
+        bool first = true;
+#pragma unroll
+        for (int h = 0; h < NI; ++h) {
+          if (!has(h)) continue;
+          uint32_t r[16];
+          tmem_ld16(taddr + h * BM + c0, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]) + __uint_as_float(r1[e]);
-        } else {
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
+          for (int e = 0; e < 16; ++e) v[e] = first ? __uint_as_float(r[e]) : v[e] + __uint_as_float(r[e]);
+          first = false;
         }
       };
       // Output of CH consecutive tokens [c0, c0 + CH) of this thread's row, already scaled.
