@@ -583,7 +583,7 @@ class NSplitWorkload:
             for j, layer in enumerate(self.fused_layers):
                 if not layer.fused:
                     raise SystemExit("cfg5 fused gather needs at least one output column per rank")
-                layer.fused_forward(self.X[j], out=self.Y[j])  # sets up the symmetric buffers (collective)
+                layer.fused_forward(self.X[j])  # sets up the symmetric buffers (collective)
             torch.cuda.synchronize()
         self.metric_kind = "gbs" if m < 512 else "tflops"
         self.unit = "GB/s" if m < 512 else "TFLOPS"
@@ -600,21 +600,22 @@ class NSplitWorkload:
     def step(self, s, st, events=None):
         ai = s % len(self.ranks_r)
         if self.fused_layers is not None:
+            # one kernel per projection; the gathered [M, N] output stays in the layer's symmetric buffer
             for j, layer in enumerate(self.fused_layers):
                 layer.w, layer.scale = self.Q[ai][j], self.S[ai][j]
-                layer.fused_forward(self.X[j], out=self.Y[j])
+                layer.fused_forward(self.X[j])
             return
         for j, ((k, n), per) in enumerate(zip(self.shapes, self.per)):
+            # one GPU: straight into Y; N-split with NCCL: into this rank's slice, then gather + relayout
+            dst, ld = (self.Y[j], n) if self.world == 1 else (self.Yloc[j], per)
             rc = self.lib.bw_w8a16_gemm(self.X[j].data_ptr(), 1, k, self.Q[ai][j].data_ptr(), k,
-                                        self.S[ai][j].data_ptr(), 0, self.Yloc[j].data_ptr(), per, self.m, per, k,
+                                        self.S[ai][j].data_ptr(), 0, dst.data_ptr(), ld, self.m, per, k,
                                         self.ws.data_ptr(), self.ws.numel(), st)
             if rc:
                 raise RuntimeError(self.lib.bw_last_error().decode())
             if self.world > 1:
                 dist.all_gather_into_tensor(self.Ygat[j], self.Yloc[j], group=self.group)
                 self.Y[j].copy_(self.Ygat[j].permute(1, 0, 2).reshape(self.m, self.world * per)[:, :n])
-            else:
-                self.Y[j].copy_(self.Yloc[j][:, :n])
 
     def e2e_setup(self):
         g = torch.Generator().manual_seed(9)

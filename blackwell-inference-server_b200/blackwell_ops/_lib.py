@@ -64,6 +64,8 @@ SIGNATURES = {
     "bw_lora_merge_requant_batched_workspace_size": (_c.c_size_t, [_c.POINTER(RequantProblem), _c.c_int]),
     "bw_lora_merge_requant_batched": (_c.c_int, [_c.POINTER(RequantProblem), _c.c_int, _P, _c.c_size_t, _P]),
     "bw_device_status": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_int), _P]),
+    "bw_quantize_kv_int8": (_c.c_int, [_P, _I64, _I64, _I64, _P, _I64, _P, _P]),
+    "bw_dequantize_kv_int8": (_c.c_int, [_P, _I64, _P, _I64, _I64, _P, _I64, _P]),
     "bw_set_wait_limit_ns": (_c.c_int, [_c.c_uint64]),
     "bw_get_wait_limit_ns": (_c.c_int, [_c.POINTER(_c.c_uint64)]),
     "bw_trace_enable": (_c.c_int, [_P, _c.c_size_t]),

@@ -205,5 +205,52 @@ def lora_merge_requant_batched(items):
     return outs
 
 
+def quantize_kv_int8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """x: [C, N] fp16 -> (q [C, N] int8, scale [C] fp32), per-channel symmetric.
+
+    scale = max|x_row| / 127 in fp32 (NaN elements ignored); q = clamp(lrint(x / scale), -127, 127).
+    Reference: quantize_kv_int8, src/blackwell_ops/cuda/kv_quant.cu:17-42, 62-76.
+    """
+    if not (x.is_cuda and x.dtype == torch.float16):
+        raise RuntimeError("x must be CUDA fp16")
+    if x.dim() != 2:
+        raise RuntimeError("x must be [C, N]")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    C, N = x.shape
+    q = torch.empty((C, N), dtype=torch.int8, device=x.device)
+    scale = torch.empty((C,), dtype=torch.float32, device=x.device)
+    if C:
+        with torch.cuda.device(x.device):
+            check(lib.bw_quantize_kv_int8(x.data_ptr(), C, N, x.stride(0), q.data_ptr(), N, scale.data_ptr(),
+                                          stream_ptr(x.device)), "quantize_kv_int8")
+    return q, scale
+
+
+def dequantize_kv_int8(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """q: [C, N] int8, scale: [C] fp32 -> x [C, N] fp16 = fp16(q * scale[:, None]).
+
+    Reference: dequantize_kv_int8, src/blackwell_ops/cuda/kv_quant.cu:47-58, 78-90.
+    """
+    if not (q.is_cuda and q.dtype == torch.int8):
+        raise RuntimeError("q must be CUDA int8")
+    if not (scale.is_cuda and scale.dtype == torch.float32):
+        raise RuntimeError("scale must be CUDA fp32")
+    if q.dim() != 2:
+        raise RuntimeError("q must be [C, N]")
+    if q.stride(1) != 1:
+        q = q.contiguous()
+    C, N = q.shape
+    if scale.numel() < C:
+        raise RuntimeError("scale must hold one value per channel")
+    scale = scale.contiguous()
+    x = torch.empty((C, N), dtype=torch.float16, device=q.device)
+    if C and N:
+        with torch.cuda.device(q.device):
+            check(lib.bw_dequantize_kv_int8(q.data_ptr(), q.stride(0), scale.data_ptr(), C, N, x.data_ptr(), N,
+                                            stream_ptr(q.device)), "dequantize_kv_int8")
+    return x
+
+
 __all__ = ["lora_delta", "lora_delta_tiled", "add_delta_", "lora_merge", "lora_merge_requant",
-           "lora_merge_requant_batched"]
+           "lora_merge_requant_batched", "quantize_kv_int8", "dequantize_kv_int8"]

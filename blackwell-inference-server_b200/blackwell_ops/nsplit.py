@@ -20,9 +20,14 @@ the tcgen05 kernel.
 ``fused=True`` replaces GEMM + NCCL all-gather by one kernel per rank
 (``bw_w8a16_gemm_allgather``): the epilogue stores every output tile into
 every rank's output buffer over peer memory (a symmetric-memory buffer, plain
-stores over NVLink) and the ranks exchange bounded completion flags.  It needs
-CUDA ranks on one node and at least one output column per rank; otherwise the
-NCCL path runs.
+16-byte stores over NVLink) and the ranks exchange bounded completion flags.
+It needs CUDA ranks on one node and at least one output column per rank;
+otherwise the NCCL path runs.  The fused call returns a view of the layer's
+symmetric output buffer, which the layer's next call overwrites (pass ``out=``
+for a copy).  ``check=True`` synchronises after each call and raises
+``DeviceTimeoutError`` if a peer flag wait ran out (a rank that did not make
+the same call); the layer's signal pads must then be reset with ``reset()``
+on every rank before its next call.
 """
 from __future__ import annotations
 
@@ -65,7 +70,7 @@ class ColumnParallelW8A16:
     def __init__(self, w_shard: torch.Tensor, scale_shard: torch.Tensor, n_total: int,
                  group: dist.ProcessGroup | None = None,
                  local_gemm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor] | None = None,
-                 fused: bool = False):
+                 fused: bool = False, check: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -82,6 +87,7 @@ class ColumnParallelW8A16:
         self.fused = (fused and self.world > 1 and local_gemm is None and w_shard.is_cuda
                       and (self.world - 1) * per < n_total)
         self._symm: dict = {}
+        self.check = check
 
     def local(self, x: torch.Tensor) -> torch.Tensor:
         return self.local_gemm(x, self.w, self.scale)
@@ -146,10 +152,24 @@ class ColumnParallelW8A16:
                 self.scale.data_ptr(), DTYPE_CODE[self.scale.dtype], yp, self.world * self.per, self.rank * self.per,
                 m, n_valid, k, sp, self.world, self.rank, ws.data_ptr() if ws is not None else None,
                 ws.numel() if ws is not None else 0, st), "int8_gemm (all-gather)")
+        if self.check:
+            from .device import check
+
+            check(x.device, "int8_gemm (all-gather)")
         if out is not None:
             out.copy_(y[:, : self.n_total])
             return out
-        return y[:, : self.n_total].clone()
+        return y[:, : self.n_total]
+
+    def reset(self) -> None:
+        """Zero this rank's signal pads (collective: every rank calls it, e.g. after a timeout)."""
+        if not self._symm:
+            return
+        group = self.group if self.group is not None else dist.group.WORLD
+        for (_, _, sig, _, _, _) in self._symm.values():
+            sig.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         if self.fused:

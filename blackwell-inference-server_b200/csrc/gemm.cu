@@ -55,7 +55,18 @@ struct GatherArgs {
                               // [2G+1] epoch of the last completed call (all zero before the first call)
   long long col0;
   int world, rank;            // world == 0: a plain GEMM into y
+  int vec;                    // 1: every Y base is 16-byte aligned and ldy, col0 are multiples of 8
 };
+
+// 8 consecutive outputs of one token row, already rounded, as one 16-byte store per rank.
+__device__ __forceinline__ void store_y8(const GatherArgs& g, void* y, int64_t idx, const uint4& v) {
+  if (g.world == 0) {
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(y) + idx) = v;
+  } else {
+    for (int r = 0; r < g.world; ++r)
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(g.y[r]) + g.col0 + idx) = v;
+  }
+}
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -629,7 +640,39 @@ __global__ void __launch_bounds__(512, 1)
       auto emit = [&](const float* v, int c0, auto ch_tag) {
         constexpr int CH = decltype(ch_tag)::value;
         if constexpr (!GLU) {
-          if (n < N) {
+          if (g.vec) {
+            // Stage the CH x 128 outputs of the chunk as dt values in shared memory (token-major),
+            // then store 16-byte rows of 8 outputs: one vector store per rank per 8 outputs instead
+            // of eight 2-byte stores.  Outputs past N (last tile) are stored element by element.
+            uint16_t* st = reinterpret_cast<uint16_t*>(xch);
+#pragma unroll
+            for (int e = 0; e < CH; ++e) {
+              if constexpr (BF16) st[e * 128 + row] = __bfloat16_as_ushort(__float2bfloat16_rn(v[e]));
+              else st[e * 128 + row] = __half_as_ushort(__float2half_rn(v[e]));
+            }
+            named_bar_sync(1, 128);
+            const int n0 = nt * 128;
+#pragma unroll
+            for (int cc = row; cc < CH * 16; cc += 128) {
+              const int e = cc >> 4, c8 = (cc & 15) * 8;
+              const int m = m0 + c0 + e;
+              if (m < M) {
+                const uint4 val = *reinterpret_cast<const uint4*>(st + e * 128 + c8);
+                const int64_t idx = static_cast<int64_t>(m) * ldy + n0 + c8;
+                if (n0 + c8 + 8 <= N) {
+                  store_y8(g, y, idx, val);
+                } else {
+                  const uint16_t* h = reinterpret_cast<const uint16_t*>(&val);
+                  for (int q8 = 0; q8 < 8 && n0 + c8 + q8 < N; ++q8) {
+                    if (g.world == 0) static_cast<uint16_t*>(y)[idx + q8] = h[q8];
+                    else
+                      for (int r = 0; r < g.world; ++r) reinterpret_cast<uint16_t*>(g.y[r])[g.col0 + idx + q8] = h[q8];
+                  }
+                }
+              }
+            }
+            named_bar_sync(1, 128);  // the stage is read before the next chunk overwrites it
+          } else if (n < N) {
 #pragma unroll
             for (int e = 0; e < CH; ++e) {
               const int m = m0 + c0 + e;
@@ -1074,6 +1117,7 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
                              const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n,
                              int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
   bw::GatherArgs g = {};
+  g.vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && ldy % 8 == 0;
   return bw::gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y, ldy, m, n, k, workspace, workspace_bytes, g,
                        stream);
 }
@@ -1122,6 +1166,8 @@ extern "C" int bw_w8a16_gemm_allgather(const void* x, int x_dtype, int64_t ldx, 
   g.col0 = col0;
   g.world = world;
   g.rank = rank;
+  g.vec = ldy % 8 == 0 && col0 % 8 == 0;
+  for (int r = 0; r < world; ++r) g.vec &= reinterpret_cast<uintptr_t>(y_ranks[r]) % 16 == 0;
   return gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y_ranks[rank], ldy, m, n, k, workspace,
                    workspace_bytes, g, stream);
 }

@@ -198,6 +198,21 @@ int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int c
                                   size_t workspace_bytes, void* stream);
 
 /*
+ * Per-channel int8 quantisation of a KV-cache tensor (the quantiser family's
+ * KV member).  Replaces quantize_kv_int8 / dequantize_kv_int8,
+ * src/blackwell_ops/cuda/kv_quant.cu:17-58 (bound at cuda/__init__.py:78-86):
+ *   x      [c, n] fp16, row stride ldx;  q [c, n] int8, row stride ldq;  scale [c] fp32
+ *   scale[i] = max_j |x[i,j]| / 127 (fp32; NaN elements ignored, 0 for a row of zeros)
+ *   q[i,j]   = clamp(lrint(x[i,j] / scale[i]), -127, 127)   (fp32 quotient, RNE, NaN -> 0)
+ *   dequantize: x'[i,j] = fp16(fp32(q[i,j]) * scale[i])
+ * Divisions are IEEE fp32.  c == 0 (or n == 0 for the dequantiser) is a no-op.
+ */
+int bw_quantize_kv_int8(const void* x, int64_t c, int64_t n, int64_t ldx, int8_t* q, int64_t ldq,
+                        float* scale, void* stream);
+int bw_dequantize_kv_int8(const int8_t* q, int64_t ldq, const float* scale, int64_t c, int64_t n,
+                          void* x, int64_t ldx, void* stream);
+
+/*
  * Device-side status of the current device: BW_OK, or BW_ERR_DEVICE_TIMEOUT
  * if a kernel's bounded wait expired since the last clear.  Synchronises
  * `stream`.  If `detail` is non-NULL it receives the failing wait site id.

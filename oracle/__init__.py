@@ -17,6 +17,8 @@ Modules
 ``lora``       ``lora_delta`` / ``lora_delta_tiled`` / ``add_delta_`` and the
                merged pipeline (reference ``src/blackwell_ops/cuda/lora_ops.cu``,
                ``src/blackwell_ops/cuda/lora_tiled.cu``).
+``kv``         the KV-cache per-channel quantiser and dequantiser
+               (reference ``src/blackwell_ops/cuda/kv_quant.cu:17-58``).
 ``inputs``     seeded synthetic inputs shared by the golden-vector script,
                the tests and the benchmarks.
 ``torch_port`` the reference's CPU PyTorch expressions, verbatim in meaning,
