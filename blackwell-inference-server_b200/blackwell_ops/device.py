@@ -14,8 +14,9 @@ without finishing its output.  This module turns that into Python errors:
   spin wait on a device (default 4 s).
 * ``Trace`` records, per CTA of each traced kernel launch, globaltimer stamps of
   its phases (start, first weight tile landed, last MMA complete, epilogue
-  done, all-gather handshake done), so a caller can see which phase bounds a
-  step.
+  done, and for the fused all-gather: stores fenced, peers ready, completion
+  handshake done; and when the preceding kernel completed), so a caller can
+  see which phase bounds a step.
 """
 from __future__ import annotations
 
@@ -82,7 +83,9 @@ def wait_limit(device=None) -> float:
     return ns.value / 1e9
 
 
-PHASES = ("start", "first_tile", "mma_done", "epilogue_done", "gather_done")
+PHASES = ("start", "first_tile", "mma_done", "epilogue_done", "stores_fenced", "peers_ready", "gather_done",
+          "predecessor_done")
+RECORD_WORDS = 16
 KERNEL_IDS = {1: "w8a16_persistent", 2: "w8a16_persistent_swiglu"}
 
 
@@ -91,7 +94,8 @@ class Launch:
     grid_id: int
     kernel: str
     ctas: int
-    stamps: torch.Tensor  # [ctas, 5] int64 ns, 0 = not reached
+    stamps: torch.Tensor  # [ctas, len(PHASES)] int64 ns, 0 = not reached
+    smid: torch.Tensor    # [ctas] SM of each CTA
 
     def phases_us(self) -> dict:
         """Phase ends relative to the first CTA start, in microseconds (max over CTAs), and
@@ -103,9 +107,9 @@ class Launch:
             col = s[:, i][s[:, i] > 0]
             if col.numel():
                 out[name] = round((float(col.max()) - t0) / 1e3, 3)
-                if name == "mma_done":  # spread of the CTAs' mainloop ends (load balance)
-                    out["mma_done_first"] = round((float(col.min()) - t0) / 1e3, 3)
-                    out["mma_done_median"] = round((float(col.median()) - t0) / 1e3, 3)
+                if col.numel() > 1:  # first CTA and median CTA: the spread shows load balance
+                    out[name + "_first"] = round((float(col.min()) - t0) / 1e3, 3)
+                    out[name + "_median"] = round((float(col.median()) - t0) / 1e3, 3)
         return out
 
 
@@ -119,7 +123,7 @@ class Trace:
 
     def __init__(self, records: int = 4096, device=None):
         self.dev = _dev(device)
-        self.buf = torch.zeros(records * 8, dtype=torch.int64, device=self.dev)
+        self.buf = torch.zeros(records * RECORD_WORDS, dtype=torch.int64, device=self.dev)
 
     def __enter__(self):
         torch.cuda.synchronize(self.dev)
@@ -136,7 +140,7 @@ class Trace:
         self.count = n.value
 
     def launches(self) -> list[Launch]:
-        rec = self.buf[: self.count * 8].view(-1, 8).cpu()
+        rec = self.buf[: self.count * RECORD_WORDS].view(-1, RECORD_WORDS).cpu()
         by_grid: dict[int, list] = {}
         for r in rec:
             by_grid.setdefault(int(r[0]), []).append(r)
@@ -145,6 +149,8 @@ class Trace:
             rows = torch.stack(rows)
             ctas = int(rows[0, 1]) >> 32
             order = torch.argsort(rows[:, 1] & 0xFFFFFFFF)
-            out.append(Launch(gid, KERNEL_IDS.get(int(rows[0, 2]), str(int(rows[0, 2]))), ctas, rows[order, 3:8]))
+            kid = int(rows[0, 2]) & 0xFFFFFFFF
+            out.append(Launch(gid, KERNEL_IDS.get(kid, str(kid)), ctas, rows[order, 3:3 + len(PHASES)],
+                              (rows[order, 2] >> 32) & 0xFFFFFFFF))
         out.sort(key=lambda l: int(l.stamps[:, 0][l.stamps[:, 0] > 0].min()))
         return out

@@ -148,11 +148,12 @@ extern "C" int bw_trace_enable(void* buffer, size_t bytes) {
   using namespace bw;
   TraceState t = {nullptr, 0u, 0u};
   if (buffer != nullptr) {
-    if (bytes < 64) return fail(BW_ERR_INVALID_ARGUMENT, "trace buffer of %zu bytes holds no record (64 bytes)", bytes);
+    if (bytes < 128)
+      return fail(BW_ERR_INVALID_ARGUMENT, "trace buffer of %zu bytes holds no record (128 bytes)", bytes);
     if (reinterpret_cast<uintptr_t>(buffer) % 8 != 0)
       return fail(BW_ERR_INVALID_ARGUMENT, "trace buffer must be 8-byte aligned");
     t.buf = static_cast<unsigned long long*>(buffer);
-    t.records = static_cast<unsigned int>(bytes / 64 > 0x7FFFFFFFu ? 0x7FFFFFFFu : bytes / 64);
+    t.records = static_cast<unsigned int>(bytes / 128 > 0x7FFFFFFFu ? 0x7FFFFFFFu : bytes / 128);
   }
   return check_cuda(cudaMemcpyToSymbol(g_trace, &t, sizeof(t)), "set trace buffer");
 }

@@ -40,9 +40,9 @@ __device__ __forceinline__ void record_timeout(int site) { atomicCAS(&g_status, 
 // ---------------------------------------------------------------------------
 // device-side phase trace (off unless bw_trace_enable gave a buffer)
 //
-// Each CTA of a traced kernel claims one 64-byte record and fills it with
+// Each CTA of a traced kernel claims one 128-byte record and fills it with
 // globaltimer stamps of its phases:
-//   u64 rec[8] = {gridid, blockIdx.x | gridDim.x << 32, kernel id, stamp[0..4]}
+//   u64 rec[16] = {gridid, blockIdx.x | gridDim.x << 32, kernel id | smid << 32, stamp[0..12]}
 // (stamp 0 = phase not reached).  The host groups records by gridid (one
 // launch) and reads the phases; nothing is written while tracing is off.
 // ---------------------------------------------------------------------------
@@ -52,7 +52,8 @@ struct TraceState {
   unsigned int next;        // next free record
 };
 extern __device__ TraceState g_trace;
-constexpr int kTraceStamps = 5;
+constexpr int kTraceStamps = 13;
+constexpr int kTraceRecordWords = 16;
 
 // Claim a record (call from one thread per CTA); null when tracing is off or full.
 __device__ __forceinline__ unsigned long long* trace_claim(int kernel_id) {
@@ -60,12 +61,14 @@ __device__ __forceinline__ unsigned long long* trace_claim(int kernel_id) {
   if (buf == nullptr) return nullptr;
   const unsigned int i = atomicAdd(&g_trace.next, 1u);
   if (i >= g_trace.records) return nullptr;
-  unsigned long long* r = buf + static_cast<size_t>(i) * 8;
+  unsigned long long* r = buf + static_cast<size_t>(i) * kTraceRecordWords;
   unsigned long long gid;
   asm volatile("mov.u64 %0, %%gridid;" : "=l"(gid));
   r[0] = gid;
   r[1] = static_cast<unsigned long long>(blockIdx.x) | (static_cast<unsigned long long>(gridDim.x) << 32);
-  r[2] = static_cast<unsigned long long>(kernel_id);
+  unsigned smid;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+  r[2] = static_cast<unsigned long long>(kernel_id) | (static_cast<unsigned long long>(smid) << 32);
   for (int e = 0; e < kTraceStamps; ++e) r[3 + e] = 0ull;
   return r;
 }

@@ -68,6 +68,8 @@ __device__ __forceinline__ void store_y8(const GatherArgs& g, void* y, int64_t i
   }
 }
 
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -585,6 +587,7 @@ __global__ void __launch_bounds__(512, 1)
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16) + C::D_COL0;
     float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH);
     pdl_wait();
+    if (warp == 10 && lane == 0) trace_stamp(trec, 7);
     bool gather_ok = true;
     uint32_t epoch = 0;
     if (g.world > 0) {
@@ -598,6 +601,7 @@ __global__ void __launch_bounds__(512, 1)
           for (int p = 0; p < g.world; ++p) st_release_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + g.rank, epoch);
         gather_ok = wait_flags(mine, g.world, epoch, kSiteGReady);
         if (!gather_ok) *abort_flag = 1;
+        trace_stamp(trec, 5);
       }
       gather_ok = !named_bar_any(1, 128, !gather_ok);
     }
@@ -796,19 +800,27 @@ __global__ void __launch_bounds__(512, 1)
     if (g.world > 0) {
       // done handshake: the last CTA of this rank tells every peer that this rank's columns
       // are in its Y, then waits until every peer has said the same (bounded)
+      // Memory order: a CTA's stores (into every rank's Y) -> bar.sync -> a GPU-scope release by
+      // its ticket thread -> the last CTA's acquire of the ticket -> its system-scope fence
+      // (cumulative: it covers every store the CTA has observed) -> the done flags, read by the
+      // peers with system-scope acquires.  Only the last CTA pays for a system-scope fence (a
+      // fence.sc.sys per CTA cost ~4 us at the end of every call on 2 GPUs).
       named_bar_sync(1, 128);
       if (warp == 10 && lane == 0) {
-        __threadfence_system();
+        fence_acq_rel_gpu();
         uint32_t* mine = reinterpret_cast<uint32_t*>(g.sig[g.rank]);
-        if (atomicAdd(mine + 2 * g.world, 1u) == gridDim.x - 1) {
+        const bool last_cta = atomicAdd(mine + 2 * g.world, 1u) == gridDim.x - 1;
+        trace_stamp(trec, 4);
+        if (last_cta) {
           // every CTA of this call has read the epoch (it took a ticket after doing so)
-          __threadfence_system();
+          fence_acq_rel_gpu();
+          fence_acq_rel_sys();
           for (int p = 0; p < g.world; ++p)
             st_release_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + g.world + g.rank, epoch);
           wait_flags(mine + g.world, g.world, epoch, kSiteGDone);
           atomicExch(mine + 2 * g.world, 0u);  // the CTA ticket, for the next call
           st_release_sys(mine + 2 * g.world + 1, epoch);
-          trace_stamp(trec, 4);
+          trace_stamp(trec, 6);
         }
       }
     }

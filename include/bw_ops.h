@@ -235,13 +235,15 @@ int bw_get_wait_limit_ns(uint64_t* ns);
 /*
  * Device-side phase trace for the current device (no reference counterpart;
  * the reference profiles with torch.profiler).  While a buffer is set, each
- * CTA of a traced kernel (the W8A16 GEMM family) claims one 64-byte record
- *   u64 {gridid, blockIdx | gridDim << 32, kernel id, t[0..4]}
+ * CTA of a traced kernel (the W8A16 GEMM family) claims one 128-byte record
+ *   u64 {gridid, blockIdx | gridDim << 32, kernel id | smid << 32, t[0..12]}
  * with globaltimer stamps (ns; 0 = phase not reached): t0 CTA start, t1 first
- * weight tile in shared memory, t2 last MMA complete, t3 epilogue done, t4
- * all-gather completion handshake done (the CTA that ran it).  buffer = NULL
- * turns tracing off; bw_trace_records gives the records written so far
- * (records past the buffer's capacity are dropped).
+ * weight tile in shared memory, t2 last MMA complete, t3 epilogue done, and
+ * for the all-gather variant t4 this CTA's stores fenced and counted, t5 the
+ * peers' ready flags seen, t6 the completion handshake done (the CTA that ran
+ * it), t7 the preceding kernel complete (griddepcontrol.wait returned).
+ * buffer = NULL turns tracing off; bw_trace_records gives the records written
+ * so far (records past the buffer's capacity are dropped).
  */
 int bw_trace_enable(void* buffer, size_t bytes);
 int bw_trace_records(unsigned int* records);
