@@ -22,6 +22,8 @@ BW_ERR_CUDA = 3
 BW_ERR_DEVICE_TIMEOUT = 4
 BW_ERR_UNSUPPORTED = 5
 
+GATHER_PAD_WORDS = 2048  # u32 words of an all-gather signal pad (include/bw_ops.h)
+
 DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 
 # Every symbol declared in include/bw_ops.h, with its ctypes signature.
@@ -52,6 +54,7 @@ SIGNATURES = {
     "bw_w8a16_gemm_static_scratch_bytes": (_c.c_size_t, []),
     "bw_w8a16_gemm_noalloc": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
                                          _P]),
+    "bw_w8a16_gemm_allgather_workspace_size": (_c.c_size_t, [_I64, _I64, _I64]),
     "bw_w8a16_gemm_allgather": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _c.POINTER(_c.c_void_p),
                                            _I64, _I64, _I64, _I64, _I64, _c.POINTER(_c.c_void_p), _c.c_int,
                                            _c.c_int, _P, _c.c_size_t, _P]),
@@ -64,6 +67,10 @@ SIGNATURES = {
     "bw_lora_merge_requant_batched_workspace_size": (_c.c_size_t, [_c.POINTER(RequantProblem), _c.c_int]),
     "bw_lora_merge_requant_batched": (_c.c_int, [_c.POINTER(RequantProblem), _c.c_int, _P, _c.c_size_t, _P]),
     "bw_device_status": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_int), _P]),
+    "bw_residual_rmsnorm": (_c.c_int, [_P, _P, _c.c_int, _I64, _P, _c.c_float, _P, _I64, _I64, _I64, _P]),
+    "bw_w8a16_gemm_rmsnorm_workspace_size": (_c.c_size_t, [_I64, _I64, _I64]),
+    "bw_w8a16_gemm_rmsnorm": (_c.c_int, [_P, _P, _c.c_int, _I64, _P, _c.c_float, _P, _I64, _P, _c.c_int, _P, _I64,
+                                         _I64, _I64, _I64, _P, _c.c_size_t, _P]),
     "bw_quantize_kv_int8": (_c.c_int, [_P, _I64, _I64, _I64, _P, _I64, _P, _P]),
     "bw_dequantize_kv_int8": (_c.c_int, [_P, _I64, _P, _I64, _I64, _P, _I64, _P]),
     "bw_set_wait_limit_ns": (_c.c_int, [_c.c_uint64]),

@@ -205,6 +205,48 @@ def lora_merge_requant_batched(items):
     return outs
 
 
+def _norm_check(x: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor | None) -> None:
+    tensors = (x, weight) if residual is None else (x, residual, weight)
+    if not all(t.is_cuda for t in tensors):
+        raise RuntimeError("inputs must be CUDA" if residual is not None else "x and w must be CUDA")
+    if x.dim() != 2:
+        raise RuntimeError("x must be [M, N]")
+    if x.dtype not in (torch.float16, torch.bfloat16) or any(t.dtype != x.dtype for t in tensors):
+        raise RuntimeError("x, residual and weight must share one dtype, fp16 or bf16")
+    if weight.numel() != x.shape[1] or (residual is not None and residual.shape != x.shape):
+        raise RuntimeError("shape mismatch")
+
+
+def fused_residual_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                           eps: float = 1e-6) -> torch.Tensor:
+    """rmsnorm(x + residual) * weight, x and residual [M, N] (reference ``cuda/__init__.py:64-67``,
+    kernel ``basic_ops.cu:49-78``): fp32 sum, the reference's summation order, IEEE fp32."""
+    _norm_check(x, weight, residual)
+    return _norm(x, residual, weight, eps)
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """rmsnorm(x) * weight, x [M, N] (reference ``cuda/__init__.py:60-61``, ``basic_ops.cu:16-46``)."""
+    _norm_check(x, weight, None)
+    return _norm(x, None, weight, eps)
+
+
+def _norm(x, residual, weight, eps):
+    from .._lib import DTYPE_CODE
+
+    x = x.contiguous()
+    residual = residual.contiguous() if residual is not None else None
+    weight = weight.contiguous()
+    M, N = x.shape
+    out = torch.empty_like(x)
+    if M and N:
+        with torch.cuda.device(x.device):
+            check(lib.bw_residual_rmsnorm(x.data_ptr(), residual.data_ptr() if residual is not None else None,
+                                          DTYPE_CODE[x.dtype], N, weight.data_ptr(), float(eps), out.data_ptr(), N,
+                                          M, N, stream_ptr(x.device)), "fused_residual_rmsnorm")
+    return out
+
+
 def quantize_kv_int8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """x: [C, N] fp16 -> (q [C, N] int8, scale [C] fp32), per-channel symmetric.
 
@@ -253,4 +295,4 @@ def dequantize_kv_int8(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
 
 
 __all__ = ["lora_delta", "lora_delta_tiled", "add_delta_", "lora_merge", "lora_merge_requant",
-           "lora_merge_requant_batched", "quantize_kv_int8", "dequantize_kv_int8"]
+           "lora_merge_requant_batched", "quantize_kv_int8", "dequantize_kv_int8", "fused_residual_rmsnorm", "rmsnorm"]

@@ -176,3 +176,48 @@ def int8_gemm_swiglu(x: torch.Tensor, w_gate: torch.Tensor, s_gate: torch.Tensor
             "int8_gemm_swiglu",
         )
     return y
+
+
+def int8_gemm_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, norm_weight: torch.Tensor,
+                      w_int8: torch.Tensor, scale: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """``int8_gemm(fused_residual_rmsnorm(x, residual, norm_weight, eps), w_int8, scale)`` in one call.
+
+    The residual + RMSNorm prologue (reference ``src/blackwell_ops/cuda/basic_ops.cu:49-78``;
+    ``residual=None`` is plain RMSNorm, ``:16-46``) normalises the rows into the GEMM's workspace
+    and the W8A16 GEMM follows with programmatic dependent launch, so its weight stream overlaps the
+    normalisation.  Bit-identical to the two ops called one after the other.  x / residual [M, K]
+    and norm_weight [K] share x's dtype (fp16 / bf16); w_int8 [N, K]; scale [N]; returns [M, N].
+    """
+    tensors = [x, norm_weight, w_int8, scale] + ([residual] if residual is not None else [])
+    if not all(t.is_cuda for t in tensors):
+        raise RuntimeError("int8_gemm_rmsnorm: all inputs must be CUDA tensors")
+    if x.dtype not in (torch.float16, torch.bfloat16) or norm_weight.dtype != x.dtype or (
+            residual is not None and residual.dtype != x.dtype):
+        raise RuntimeError("int8_gemm_rmsnorm: x, residual and norm_weight must share fp16 or bf16")
+    if w_int8.dtype != torch.int8 or scale.dtype not in DTYPE_CODE:
+        raise RuntimeError("int8_gemm_rmsnorm: w_int8 must be int8 and scale fp16 / bf16 / fp32")
+    if x.dim() != 2 or w_int8.dim() != 2 or w_int8.shape[1] != x.shape[1] or norm_weight.numel() != x.shape[1]:
+        raise RuntimeError("int8_gemm_rmsnorm: x must be [M, K], norm_weight [K] and w_int8 [N, K]")
+    if residual is not None and residual.shape != x.shape:
+        raise RuntimeError("int8_gemm_rmsnorm: residual must match x")
+    M, K = x.shape
+    N = w_int8.shape[0]
+    if scale.numel() != N:
+        raise RuntimeError(f"int8_gemm_rmsnorm: scale must have N={N} elements")
+    x = x.contiguous()
+    residual = residual.contiguous() if residual is not None else None
+    w_int8 = w_int8.contiguous()
+    scale = scale.reshape(N).contiguous()
+    norm_weight = norm_weight.contiguous()
+    y = torch.empty(M, N, device=x.device, dtype=x.dtype)
+    if M == 0 or N == 0:
+        return y
+    with torch.cuda.device(x.device):
+        st = stream_ptr(x.device)
+        nbytes = lib.bw_w8a16_gemm_rmsnorm_workspace_size(M, N, K)
+        ws = _workspace(x.device, st, nbytes)
+        check(lib.bw_w8a16_gemm_rmsnorm(x.data_ptr(), residual.data_ptr() if residual is not None else None,
+                                        DTYPE_CODE[x.dtype], K, norm_weight.data_ptr(), float(eps), w_int8.data_ptr(),
+                                        K, scale.data_ptr(), DTYPE_CODE[scale.dtype], y.data_ptr(), N, M, N, K,
+                                        ws.data_ptr(), ws.numel(), st), "int8_gemm_rmsnorm")
+    return y

@@ -83,9 +83,8 @@ class ColumnParallelW8A16:
         self.per = per
         self.local_gemm = local_gemm or _default_gemm()
         self._use_into_tensor = True
-        # fused all-gather: every rank must own at least one real column (the same decision on all ranks)
-        self.fused = (fused and self.world > 1 and local_gemm is None and w_shard.is_cuda
-                      and (self.world - 1) * per < n_total)
+        # fused all-gather: CUDA ranks with the library's kernel (the same decision on all ranks)
+        self.fused = fused and self.world > 1 and local_gemm is None and w_shard.is_cuda
         self._symm: dict = {}
         self.check = check
 
@@ -121,7 +120,9 @@ class ColumnParallelW8A16:
                 enable(group.group_name)
             y = symm_mem.empty((m, self.world * self.per), dtype=dtype, device=device)
             hy = symm_mem.rendezvous(y, group.group_name)
-            sig = symm_mem.empty((64,), dtype=torch.int32, device=device)
+            from ._lib import GATHER_PAD_WORDS
+
+            sig = symm_mem.empty((GATHER_PAD_WORDS,), dtype=torch.int32, device=device)
             sig.zero_()
             hs = symm_mem.rendezvous(sig, group.group_name)
             torch.cuda.synchronize(device)
@@ -141,16 +142,17 @@ class ColumnParallelW8A16:
         if x.stride(1) != 1:
             x = x.contiguous()
         m, k = x.shape
-        n_valid = min(self.per, self.n_total - self.rank * self.per)
+        # every rank computes its whole padded shard (per rows; the rows past N are zero weights
+        # whose outputs land in the buffer's padding columns), so all ranks run the same plan
         y, _, _, _, yp, sp = self._fused_buffers(m, x.dtype, x.device)
         st = stream_ptr(x.device)
-        need = lib.bw_w8a16_gemm_workspace_size(m, n_valid, k)
+        need = lib.bw_w8a16_gemm_allgather_workspace_size(m, self.per, k)
         ws = _workspace(x.device, st, need)
         with torch.cuda.device(x.device):
             check(lib.bw_w8a16_gemm_allgather(
                 x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0), self.w.data_ptr(), self.w.stride(0),
                 self.scale.data_ptr(), DTYPE_CODE[self.scale.dtype], yp, self.world * self.per, self.rank * self.per,
-                m, n_valid, k, sp, self.world, self.rank, ws.data_ptr() if ws is not None else None,
+                m, self.per, k, sp, self.world, self.rank, ws.data_ptr() if ws is not None else None,
                 ws.numel() if ws is not None else 0, st), "int8_gemm (all-gather)")
         if self.check:
             from .device import check

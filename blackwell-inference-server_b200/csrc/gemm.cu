@@ -51,12 +51,16 @@ __device__ __forceinline__ void store_out(void* y, int64_t idx, float v) {
 // stores), guarded by two flag handshakes on the ranks' signal pads.
 struct GatherArgs {
   unsigned long long y[8];    // each rank's Y [M, ldy]; this rank's columns start at col0
-  unsigned long long sig[8];  // each rank's signal pad (u32): [0,G) ready, [G,2G) done, [2G] CTA ticket,
-                              // [2G+1] epoch of the last completed call (all zero before the first call)
+  unsigned long long sig[8];  // each rank's signal pad (u32, kGatherPadWords): [0,G) ready flags, [G] CTA
+                              // ticket, [G+1] epoch of the last call, [kGatherDone0 + b*8 + p] CTA b of rank
+                              // p has stored its outputs (all zero before the first call)
   long long col0;
   int world, rank;            // world == 0: a plain GEMM into y
   int vec;                    // 1: every Y base is 16-byte aligned and ldy, col0 are multiples of 8
 };
+
+constexpr int kGatherDone0 = 64;      // first per-CTA done flag of a signal pad
+constexpr int kGatherPadWords = 2048;  // u32 words of a signal pad: room for 248 CTAs x 8 ranks
 
 // 8 consecutive outputs of one token row, already rounded, as one 16-byte store per rank.
 __device__ __forceinline__ void store_y8(const GatherArgs& g, void* y, int64_t idx, const uint4& v) {
@@ -68,8 +72,10 @@ __device__ __forceinline__ void store_y8(const GatherArgs& g, void* y, int64_t i
   }
 }
 
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -161,8 +167,9 @@ struct PCfg {
   static constexpr int X_BYTES = 2 * X_PANEL;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
   static constexpr int NI = BM <= 32 ? BW_GEMM_DEC_ISSUERS : BM == 64 ? 2 : 1;
-  // the producer of the weight tiles also loads the activation tiles (else warp 15 does)
-  static constexpr bool ONE_PRODUCER = NI >= 3;
+  // with three issuers warp 15 is an issuer and each issuer loads the activation tiles of its own
+  // k-blocks ahead of its MMAs (else warp 15 loads them all)
+  static constexpr bool ISSUER_X = NI >= 3;
   // Prefill ring: weight + activation tiles per stage, up to 4 stages of 48 KB.
   static constexpr int STAGES_PRE = (220 * 1024) / STAGE_BYTES > 8 ? 8 : (220 * 1024) / STAGE_BYTES;
   // Decode rings.  The weight stream is bound by the bytes a CTA keeps in flight (Little's law:
@@ -197,7 +204,7 @@ struct PCfg {
   static_assert(ASTAGES >= 2, "TMEM A buffers");
   static_assert(D_COL0 + DBUF * NI * BM <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(!ONE_PRODUCER || XSTAGES >= STAGES + ASTAGES, "activation ring must not stall the producer");
+  static_assert(!ISSUER_X || XSTAGES >= 2 * NI, "activation ring too shallow for the issuers' look-ahead");
   static_assert((2 * STAGES + 2 * XSTAGES + 2 * ASTAGES + 4 + 1) * 8 + 32 <= BAR_BYTES, "barrier area");
   static_assert(X_PANEL % 1024 == 0 && OFF_X % 1024 == 0, "128-byte swizzled x tiles are 1024-byte aligned");
 };
@@ -375,39 +382,16 @@ __global__ void __launch_bounds__(512, 1)
   }
 
   if (warp == 0) {
-    // ---------------- TMA producer: weight tiles (and, with ONE_PRODUCER, activation tiles) ----------------
-    // Weights do not depend on the preceding kernel: the first ring of weight tiles is issued
-    // before griddepcontrol.wait, and a slot is free as soon as a dequantiser group has read it
-    // into registers.  Activation tiles follow their k-block's weight tile in the TMA queue.
+    // ---------------- TMA producer: weight tiles ----------------
+    // Weights do not depend on the preceding kernel (no griddepcontrol.wait here), and a
+    // slot is free as soon as a dequantiser group has read it into registers.
     if (lane == 0) {
       // a weight tile used by several M-tiles stays in L2 for the CTAs that share it
       const uint64_t pol_w = sc.m_tiles > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
-      const uint64_t pol_x = l2_policy_evict_last();
-      int it = 0, jx = 0, ix = 0;
-      bool ok = true, waited = !C::ONE_PRODUCER, xseg = false;
-      SegWalk wk(sc, blockIdx.x, gridDim.x), wx(sc, blockIdx.x, gridDim.x);
-      Seg sg, sx;
-      // activation tiles of k-blocks [jx, upto)
-      auto load_x_until = [&](int upto) {
-        while (ok && jx < upto) {
-          if (!xseg || ix >= sx.nkb) {
-            xseg = wx.next(sc, sx);
-            ix = 0;
-            if (!xseg) return;
-          }
-          const int xs = jx % XSTAGES;
-          if (jx >= XSTAGES && !mbar_wait(&xempty[xs], ((jx / XSTAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
-            ok = false;
-            return;
-          }
-          const int kx = (sx.k0 + ix) * C::BK, m0 = (sx.t % sc.m_tiles) * BM;
-          mbar_arrive_expect_tx(&xfull[xs], C::X_BYTES);
-          tma_load_2d(sX + xs * C::X_BYTES, &tm_x, &xfull[xs], kx, m0, pol_x);
-          tma_load_2d(sX + xs * C::X_BYTES + C::X_PANEL, &tm_x, &xfull[xs], kx + 64, m0, pol_x);
-          ++ix;
-          ++jx;
-        }
-      };
+      int it = 0;
+      bool ok = true;
+      SegWalk wk(sc, blockIdx.x, gridDim.x);
+      Seg sg;
       while (ok && wk.next(sc, sg)) {
         const int nt = sg.t / sc.m_tiles;
         for (int i = 0; i < sg.nkb; ++i, ++it) {
@@ -423,31 +407,13 @@ __global__ void __launch_bounds__(512, 1)
           } else {
             tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 128, pol_w);
           }
-          if constexpr (C::ONE_PRODUCER) {
-            if (!waited && it + 1 >= STAGES) {
-              pdl_wait();
-              waited = true;
-            }
-            if (waited) load_x_until(it + 1);
-          }
         }
       }
-      if constexpr (C::ONE_PRODUCER) {
-        if (ok && !waited) {  // fewer k-blocks than ring slots
-          pdl_wait();
-          waited = true;
-        }
-        load_x_until(it);
-      }
-      if (!ok) {  // wait (bounded) for the copies still in flight into this CTA's shared memory
+      if (!ok)  // wait (bounded) for the copies still in flight into this CTA's shared memory
         for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
           mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
-        if constexpr (C::ONE_PRODUCER)
-          for (int j = (jx > XSTAGES ? jx - XSTAGES : 0); j < jx; ++j)
-            mbar_wait(&xfull[j % XSTAGES], (j / XSTAGES) & 1, nullptr, kSitePDrain);
-      }
     }
-  } else if (warp == 15 && !C::ONE_PRODUCER) {
+  } else if (warp == 15 && !C::ISSUER_X) {
     // ---------------- TMA producer: activation tiles (after the predecessor) ----------------
     if (lane == 0) {
       const uint64_t pol_x = l2_policy_evict_last();
@@ -486,6 +452,36 @@ __global__ void __launch_bounds__(512, 1)
       bool ok = true;
       SegWalk wk(sc, blockIdx.x, gridDim.x);
       Seg sg;
+      // ISSUER_X: this issuer's activation tiles (k-blocks jx = h, h + NI, ...), loaded ahead of its
+      // MMAs; a slot is refilled once the MMAs of the k-block that last used it have completed.
+      int jx = h, xbase = 0, xcons = h;  // xcons: this issuer's next k-block whose tile it has not waited for
+      bool xseg = false;
+      SegWalk wx(sc, blockIdx.x, gridDim.x);
+      Seg sx = {0, 0, 0, 0};
+      const uint64_t pol_x = l2_policy_evict_last();
+      // 1: loaded, 0: slot still busy (non-blocking attempt), -1: no such k-block or abort
+      auto load_x = [&](int jj, bool block) -> int {
+        const int xs = jj % XSTAGES;
+        const uint32_t par = ((jj / XSTAGES) & 1) ^ 1;
+        if (jj >= XSTAGES) {
+          if (block) {
+            if (!mbar_wait(&xempty[xs], par, abort_flag, kSitePProd)) return -1;
+          } else if (!mbar_try_wait(&xempty[xs], par)) {
+            return 0;
+          }
+        }
+        while (!xseg || jj >= xbase + sx.nkb) {
+          if (xseg) xbase += sx.nkb;
+          xseg = wx.next(sc, sx);
+          if (!xseg) return -1;
+        }
+        const int kx = (sx.k0 + (jj - xbase)) * C::BK, m0 = (sx.t % sc.m_tiles) * BM;
+        mbar_arrive_expect_tx(&xfull[xs], C::X_BYTES);
+        tma_load_2d(sX + xs * C::X_BYTES, &tm_x, &xfull[xs], kx, m0, pol_x);
+        tma_load_2d(sX + xs * C::X_BYTES + C::X_PANEL, &tm_x, &xfull[xs], kx + 64, m0, pol_x);
+        return 1;
+      };
+      if constexpr (C::ISSUER_X) pdl_wait();  // activations may come from the preceding kernel
       for (; ok && wk.next(sc, sg); ++j) {
         const int b = j % DBUF;
         if (!mbar_wait(&dempty[b], ((j / DBUF) & 1) ^ 1, abort_flag, kSitePMmaD)) break;
@@ -494,6 +490,12 @@ __global__ void __launch_bounds__(512, 1)
         uint32_t acc = 0;  // 0 until this issuer's first MMA of the segment
         for (int i = 0; i < sg.nkb; ++i, ++it) {
           if (NI > 1 && it % NI != h) continue;
+          if constexpr (C::ISSUER_X) {
+            for (; ok && jx <= it; jx += NI) ok = load_x(jx, true) > 0;  // this k-block's tile, at least
+            for (; ok && jx <= it + XSTAGES - NI; jx += NI)               // and ahead while slots are free
+              if (load_x(jx, false) <= 0) break;
+            if (!ok) break;
+          }
           const int s = it % XSTAGES;
           const uint32_t ph = (it / XSTAGES) & 1;
           const int t = it % ASTAGES;
@@ -502,6 +504,7 @@ __global__ void __launch_bounds__(512, 1)
             ok = false;
             break;
           }
+          xcons = it + NI;
           tc_fence_after();
           const uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
 #pragma unroll
@@ -514,6 +517,12 @@ __global__ void __launch_bounds__(512, 1)
           umma_commit(&aempty[t]);
         }
         if (ok) umma_commit(&dfull[b]);
+      }
+      if constexpr (C::ISSUER_X) {
+        // activation tiles this issuer loaded and never waited for (after an abort) land before the
+        // CTA may exit (the look-ahead loads nothing past the CTA's last k-block)
+        for (int jj = xcons; jj < jx; jj += NI)
+          mbar_wait(&xfull[jj % XSTAGES], (jj / XSTAGES) & 1, nullptr, kSitePDrain);
       }
       // every issued MMA has completed before TMEM is released
       umma_commit(final_bar);
@@ -595,8 +604,14 @@ __global__ void __launch_bounds__(512, 1)
       // graph replays correctly); ready handshake: this rank's Y may be overwritten now (its
       // earlier readers are done), and no store goes to a peer before that peer has said the same
       if (warp == 10 && lane == 0) {
-        const uint32_t* mine = reinterpret_cast<const uint32_t*>(g.sig[g.rank]);
-        epoch = ld_acquire_sys(mine + 2 * g.world + 1) + 1u;
+        uint32_t* mine = reinterpret_cast<uint32_t*>(g.sig[g.rank]);
+        epoch = ld_acquire_sys(mine + g.world + 1) + 1u;
+        // the last CTA to read the epoch stores it as this call's (the next call reads it after
+        // this grid has completed) and resets the ticket
+        if (atomicAdd(mine + g.world, 1u) == gridDim.x - 1) {
+          atomicExch(mine + g.world, 0u);
+          atomicExch(mine + g.world + 1, epoch);
+        }
         if (blockIdx.x == 0)
           for (int p = 0; p < g.world; ++p) st_release_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + g.rank, epoch);
         gather_ok = wait_flags(mine, g.world, epoch, kSiteGReady);
@@ -800,28 +815,21 @@ __global__ void __launch_bounds__(512, 1)
     if (g.world > 0) {
       // done handshake: the last CTA of this rank tells every peer that this rank's columns
       // are in its Y, then waits until every peer has said the same (bounded)
-      // Memory order: a CTA's stores (into every rank's Y) -> bar.sync -> a GPU-scope release by
-      // its ticket thread -> the last CTA's acquire of the ticket -> its system-scope fence
-      // (cumulative: it covers every store the CTA has observed) -> the done flags, read by the
-      // peers with system-scope acquires.  Only the last CTA pays for a system-scope fence (a
-      // fence.sc.sys per CTA cost ~4 us at the end of every call on 2 GPUs).
+      // Completion, CTA by CTA: CTA b of this rank tells CTA b of every rank that its outputs are
+      // stored, then waits for the same word from CTA b of every peer (every rank runs the same
+      // grid), so when every CTA of a rank is past its wait, every peer's outputs are in its Y.
+      // Memory order: the CTA's stores -> bar.sync -> a system-scope fence by the flag thread
+      // (cumulative over the stores the barrier made it observe) -> the flags; readers acquire.
+      // The fences of the CTAs run side by side as each CTA finishes, not at the end of the call.
       named_bar_sync(1, 128);
       if (warp == 10 && lane == 0) {
-        fence_acq_rel_gpu();
-        uint32_t* mine = reinterpret_cast<uint32_t*>(g.sig[g.rank]);
-        const bool last_cta = atomicAdd(mine + 2 * g.world, 1u) == gridDim.x - 1;
+        fence_acq_rel_sys();
+        for (int p = 0; p < g.world; ++p)
+          st_relaxed_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + kGatherDone0 + blockIdx.x * 8 + g.rank, epoch);
         trace_stamp(trec, 4);
-        if (last_cta) {
-          // every CTA of this call has read the epoch (it took a ticket after doing so)
-          fence_acq_rel_gpu();
-          fence_acq_rel_sys();
-          for (int p = 0; p < g.world; ++p)
-            st_release_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + g.world + g.rank, epoch);
-          wait_flags(mine + g.world, g.world, epoch, kSiteGDone);
-          atomicExch(mine + 2 * g.world, 0u);  // the CTA ticket, for the next call
-          st_release_sys(mine + 2 * g.world + 1, epoch);
-          trace_stamp(trec, 6);
-        }
+        const uint32_t* mine = reinterpret_cast<const uint32_t*>(g.sig[g.rank]);
+        if (gather_ok && !*abort_flag) wait_flags(mine + kGatherDone0 + blockIdx.x * 8, g.world, epoch, kSiteGDone);
+        trace_stamp(trec, 6);
       }
     }
   }
@@ -892,7 +900,9 @@ struct GemmPlan {
 // the split count; when CTAs would walk several units each, stream-K (mode 1)
 // removes the last round's imbalance (e.g. 1187 LM-head tiles on 148 SMs:
 // 9 units for some CTAs against 8.02 on average).
-static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false) {
+// gather = true (the fused all-gather): stream-K over all SMs whatever the shape, so every rank
+// runs the same grid (its CTAs pair up with the peers' CTAs of the same index).
+static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false, bool gather = false) {
   GemmPlan p;
   const int sms = num_sms();
   const int rows = glu ? 64 : 128;  // output columns per tile
@@ -928,22 +938,25 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false) {
   // prefill tiles (BM = 128) keep split-K units unless forced: measured 809 against 784 TFLOPS on
   // the Llama-3-8B MLP, as the 64 KB pieces of cut tiles and their end-of-range reductions cost
   // more than the last round's imbalance
-  if (BW_GEMM_STREAMK && ((best_per_cta >= 2 && p.bm < 128) || force_sk) && p.work >= sms &&
-      p.work * sms < (1LL << 31)) {
+  if (BW_GEMM_STREAMK && ((best_per_cta >= 2 && p.bm < 128) || force_sk || gather) &&
+      (p.work >= sms || gather) && p.work * sms < (1LL << 31)) {
     const int64_t per = (p.work + sms - 1) / sms;
     const double seg = static_cast<double>((per + p.kblocks - 1) / p.kblocks + 1);
     const double cost = per * 16384.0 + seg * 6000.0 + 2.0 * part_cost;
-    if (cost < best || force_sk) {
+    if (cost < best || force_sk || gather) {
+      // every CTA's range must hold at least one k-block (the owner arithmetic assumes it), so
+      // a gather plan with less work than SMs runs one CTA per k-block
+      const int grid = p.work < sms ? static_cast<int>(p.work) : sms;
       p.mode = 1;
-      p.grid = sms;
+      p.grid = grid;
       p.splits = 1;
       p.kb_per_split = p.kblocks;
       p.units = 0;
       bool cut = false;  // does a range boundary fall inside a tile?
-      for (int b = 1; b < sms && !cut; ++b) cut = (static_cast<int64_t>(b) * p.work / sms) % p.kblocks != 0;
+      for (int b = 1; b < grid && !cut; ++b) cut = (static_cast<int64_t>(b) * p.work / grid) % p.kblocks != 0;
       if (cut) {
         p.counter_bytes = kGemmCounterBytes;
-        p.partial_bytes = static_cast<size_t>(sms) * 2 * 128 * p.bm * sizeof(float);
+        p.partial_bytes = static_cast<size_t>(grid) * 2 * 128 * p.bm * sizeof(float);
       }
       return p;
     }
@@ -1033,6 +1046,12 @@ extern "C" size_t bw_w8a16_gemm_workspace_size(int64_t m, int64_t n, int64_t k) 
   return p.counter_bytes + p.partial_bytes;
 }
 
+extern "C" size_t bw_w8a16_gemm_allgather_workspace_size(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  const bw::GemmPlan p = bw::plan_gemm(m, n, k, false, true);
+  return p.counter_bytes + p.partial_bytes;
+}
+
 extern "C" size_t bw_w8a16_gemm_workspace_zeroed_bytes(int64_t m, int64_t n, int64_t k) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;
   return bw::plan_gemm(m, n, k).counter_bytes;
@@ -1083,9 +1102,12 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
     return check_launch("w8a16_simt_kernel");
   }
 
-  const GemmPlan p = plan_gemm(m, n, k, glu);
+  const GemmPlan p = plan_gemm(m, n, k, glu, g.world > 0);
   if (p.units < 0) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: m=%lld n=%lld is too many output tiles",
                                (long long)m, (long long)n);
+  if (g.world > 0 && (p.mode != 1 || p.grid > (kGatherPadWords - kGatherDone0) / 8))
+    return fail(BW_ERR_UNSUPPORTED, "int8_gemm (all-gather): shape m=%lld n=%lld k=%lld has no stream-K plan",
+                (long long)m, (long long)n, (long long)k);
   float* ws = nullptr;
   int* counters = nullptr;
   if (p.partial_bytes > 0) {

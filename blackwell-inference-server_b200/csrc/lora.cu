@@ -190,6 +190,229 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent ΔW / merge: one CTA per SM walks a contiguous range of 128 x 128 output tiles in
+// row-major order, so a CTA keeps the row block's B[128, r] resident across its k-tiles and
+// streams only A[r, 128] panels (from L2: A is shared by every row block) and, for the merge,
+// the W tiles.  The MMA of tile i+1 runs while the epilogue of tile i converts and stores it
+// (double-buffered TMEM accumulators), and TMA stores overlap the next tile's epilogue.
+//   warp 0      TMA producer (B when the row block changes, A panels, W tiles)
+//   warp 1      TMEM owner and tcgen05.mma issuer (r/16 MMAs of M=N=128, K=16 per tile)
+//   warps 4-11  epilogue, two groups of four taking alternate tiles, thread = row: fp16(acc * s)
+//               (delta) or fp16(W + fp16(acc * s)) (merge), staged in the 128-byte-swizzled
+//               layout and written by TMA stores
+// The arithmetic is lora_tile_epilogue's, so the output bits equal lora_tc_kernel's.
+// ---------------------------------------------------------------------------
+struct LoraStreamSmem {
+  int rp, nbp, a_bytes, b_bytes, wslots, aslots, off_a, off_b, off_w, off_bar, total;
+  __host__ __device__ LoraStreamSmem(int r, int mode) {
+    rp = (r + 15) / 16 * 16;
+    nbp = (rp + 63) / 64;
+    a_bytes = ((2 * rp * 128 + 1023) / 1024) * 1024;
+    b_bytes = nbp * 16384;
+    wslots = mode == kModeDelta ? 2 : 3;  // output staging, one per epilogue group (delta) / W tiles
+                                          // updated in place, one ahead of the two groups (merge)
+    const int left = 200 * 1024 - b_bytes - wslots * 32768;
+    aslots = left / a_bytes > 6 ? 6 : left / a_bytes;
+    off_a = 0;
+    off_b = off_a + aslots * a_bytes;
+    off_w = off_b + b_bytes;
+    off_bar = off_w + wslots * 32768;
+    total = off_bar + 256 + 1024;
+  }
+};
+
+enum LoraStreamSite : int {
+  kSiteLsProd = 221,
+  kSiteLsMma = 222,
+  kSiteLsEpi = 223,
+  kSiteLsDrain = 224,
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(384, 1)
+    lora_stream_kernel(const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
+                       const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_out, int N,
+                       int K, int r, float scaling) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const LoraStreamSmem L(r, MODE);
+  const int SA = L.aslots, SW = L.wslots;
+  uint64_t* afull = reinterpret_cast<uint64_t*>(smem + L.off_bar);  // [6]
+  uint64_t* aempty = afull + 6;                                      // [6]
+  uint64_t* bfull = aempty + 6;
+  uint64_t* bempty = bfull + 1;
+  uint64_t* wfull = bempty + 1;   // [3] merge: W tile landed
+  uint64_t* wempty = wfull + 3;   // [3] merge: the TMA store of the tile has read the slot
+  uint64_t* dfull = wempty + 3;   // [2]
+  uint64_t* dempty = dfull + 2;   // [2]
+  uint64_t* final_bar = dempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_cb = (K + 127) / 128;
+  const long long tiles = static_cast<long long>((N + 127) / 128) * n_cb;
+  const long long t_begin = tiles * blockIdx.x / gridDim.x, t_end = tiles * (blockIdx.x + 1) / gridDim.x;
+  const int ntile = static_cast<int>(t_end - t_begin);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 6; ++i) {
+      mbar_init(&afull[i], 1);
+      mbar_init(&aempty[i], 1);
+    }
+    mbar_init(bfull, 1);
+    mbar_init(bempty, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wempty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], 4);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t keep = l2_policy_evict_last();   // A and B are re-read by many tiles
+      const uint64_t once = l2_policy_evict_first();  // W is read once
+      int prev_rb = -1, nb = 0, issued_a = 0, issued_w = 0;
+      bool ok = true;
+      for (int i = 0; i < ntile && ok; ++i) {
+        const long long t = t_begin + i;
+        const int rb = static_cast<int>(t / n_cb), cb = static_cast<int>(t % n_cb);
+        if (rb != prev_rb) {  // new row block: B once the MMAs of the previous one are done
+          if (nb > 0 && !mbar_wait(bempty, (nb - 1) & 1, abort_flag, kSiteLsProd)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bfull, L.b_bytes);
+          for (int p = 0; p < L.nbp; ++p) tma_load_2d(smem + L.off_b + p * 16384, &tm_b, bfull, p * 64, rb * 128, keep);
+          ++nb;
+          prev_rb = rb;
+        }
+        const int sa = i % SA;
+        if (i >= SA && !mbar_wait(&aempty[sa], ((i / SA) & 1) ^ 1, abort_flag, kSiteLsProd)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sA = smem + L.off_a + sa * L.a_bytes;
+        mbar_arrive_expect_tx(&afull[sa], 2 * L.rp * 128);
+        tma_load_2d(sA, &tm_a, &afull[sa], cb * 128, 0, keep);
+        tma_load_2d(sA + L.rp * 128, &tm_a, &afull[sa], cb * 128 + 64, 0, keep);
+        issued_a = i + 1;
+        if constexpr (MODE != kModeDelta) {
+          const int sw = i % SW;
+          if (i >= SW && !mbar_wait(&wempty[sw], ((i / SW) & 1) ^ 1, abort_flag, kSiteLsProd)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sWt = smem + L.off_w + sw * 32768;
+          mbar_arrive_expect_tx(&wfull[sw], 32768);
+          tma_load_2d(sWt, &tm_w, &wfull[sw], cb * 128, rb * 128, once);
+          tma_load_2d(sWt + 16384, &tm_w, &wfull[sw], cb * 128 + 64, rb * 128, once);
+          issued_w = i + 1;
+        }
+      }
+      if (!ok) {  // the copies still in flight land before the CTA may exit
+        for (int j = issued_a > SA ? issued_a - SA : 0; j < issued_a; ++j)
+          mbar_wait(&afull[j % SA], (j / SA) & 1, nullptr, kSiteLsDrain);
+        for (int j = issued_w > SW ? issued_w - SW : 0; j < issued_w; ++j)
+          mbar_wait(&wfull[j % SW], (j / SW) & 1, nullptr, kSiteLsDrain);
+        if (nb > 0) mbar_wait(bfull, (nb - 1) & 1, nullptr, kSiteLsDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(128, 128, false, true);
+      int prev_rb = -1, nb = 0;
+      for (int i = 0; i < ntile; ++i) {
+        const long long t = t_begin + i;
+        const int rb = static_cast<int>(t / n_cb);
+        const int db = i & 1;
+        if (!mbar_wait(&dempty[db], ((i >> 1) & 1) ^ 1, abort_flag, kSiteLsMma)) break;
+        if (rb != prev_rb) {
+          if (!mbar_wait(bfull, nb & 1, abort_flag, kSiteLsMma)) break;
+          ++nb;
+          prev_rb = rb;
+        }
+        const int sa = i % SA;
+        if (!mbar_wait(&afull[sa], (i / SA) & 1, abort_flag, kSiteLsMma)) break;
+        tc_fence_after();
+        const uint32_t b_base = smem_u32(smem + L.off_b);
+        const uint32_t a_base = smem_u32(smem + L.off_a + sa * L.a_bytes);
+        for (int kk = 0; kk < L.rp / 16; ++kk) {
+          const uint64_t ad = make_sdesc(b_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          const uint64_t bd = make_sdesc(a_base + kk * 2048, L.rp * 128, 1024, kLayoutSW128);
+          umma_f16(tmem + db * 128, ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&aempty[sa]);
+        umma_commit(&dfull[db]);
+        // the last tile of this row block in the CTA's range: B may be replaced once it completes
+        const bool last_of_rb = i + 1 == ntile || static_cast<int>((t + 1) / n_cb) != rb;
+        if (last_of_rb) umma_commit(bempty);
+      }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, nullptr, kSiteLsDrain);
+    }
+  } else if (warp >= 4) {
+    // two epilogue groups (warps 4-7, 8-11) take alternate tiles, each with its own accumulator
+    // buffer (tile i: buffer i & 1) and named barrier; a group's leader issues its TMA stores and
+    // waits for them to read the staging slot before the group writes that slot again
+    const int grp = (warp - 4) >> 2;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int bar_id = 1 + grp;
+    const bool leader = (warp & 3) == 0 && lane == 0 && (warp >> 2) == 1 + grp;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    for (int i = grp; i < ntile; i += 2) {
+      const long long t = t_begin + i;
+      const int rb = static_cast<int>(t / n_cb), cb = static_cast<int>(t % n_cb);
+      const int db = i & 1;
+      const int sw = i % SW;
+      uint8_t* sWt = smem + L.off_w + sw * 32768;
+      bool ok = mbar_wait(&dfull[db], (i >> 1) & 1, abort_flag, kSiteLsEpi);
+      if constexpr (MODE != kModeDelta) ok = ok && mbar_wait(&wfull[sw], (i / SW) & 1, abort_flag, kSiteLsEpi);
+      // one decision for the group; the leader's wait for its previous store is ordered before it
+      if (named_bar_any(bar_id, 128, !ok || *abort_flag)) break;
+      tc_fence_after();
+      lora_tile_epilogue<MODE>(lane_base + db * 128, sWt, row, scaling);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dempty[db]);  // accumulator read: the MMA may reuse it
+      fence_proxy_async_smem();
+      named_bar_sync(bar_id, 128);
+      if (leader) {
+        tma_store_2d(&tm_out, sWt, cb * 128, rb * 128);
+        if (cb * 128 + 64 < K) tma_store_2d(&tm_out, sWt + 16384, cb * 128 + 64, rb * 128);  // never past K
+        tma_store_commit();
+        tma_store_wait_read0();  // the store has read the slot
+        if constexpr (MODE != kModeDelta) mbar_arrive(&wempty[sw]);
+      }
+    }
+    if (leader) tma_store_wait0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Grouped, cooperative merge + requantisation.
 //
 // One launch covers up to kReqMaxProblems projections (e.g. every projection an
@@ -769,6 +992,26 @@ static int launch_lora_tc(const CUtensorMap& tb, const CUtensorMap& ta, const CU
   return check_launch("lora_tc_kernel");
 }
 
+template <int MODE>
+static int launch_lora_stream(const CUtensorMap& tb, const CUtensorMap& ta, const CUtensorMap& tw,
+                              const CUtensorMap& to, int N, int K, int r, float s, cudaStream_t st) {
+  const LoraStreamSmem L(r, MODE);
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    // every rank's layout fits in the 200 KB planning budget plus barriers and alignment slack
+    err[dev & 63] = cudaFuncSetAttribute(lora_stream_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024 + 256 + 1024);
+  });
+  if (int rc = check_cuda(err[dev & 63], "cudaFuncSetAttribute(lora_stream_kernel)")) return rc;
+  const long long tiles = static_cast<long long>((N + 127) / 128) * ((K + 127) / 128);
+  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+  lora_stream_kernel<MODE><<<grid, 384, L.total, st>>>(tb, ta, tw, to, N, K, r, s);
+  return check_launch("lora_stream_kernel");
+}
+
 static int lora_maps(CUtensorMap* tb, CUtensorMap* ta, const void* a, const void* b, int64_t n, int64_t k, int64_t r) {
   const int rp = static_cast<int>((r + 15) / 16 * 16);
   if (int s = make_tmap_2d(tb, b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n, r, r * 2, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -944,7 +1187,7 @@ extern "C" int bw_lora_delta(const void* a, const void* b, void* delta, int64_t 
   if (int s = lora_maps(&tb, &ta, a, b, n, k, r)) return s;
   if (int s = make_tmap_2d(&to, delta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n, k, k * 2, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
-  return launch_lora_tc<kModeDelta>(tb, ta, to, to, (int)n, (int)k, (int)r, scaling, st);
+  return launch_lora_stream<kModeDelta>(tb, ta, to, to, (int)n, (int)k, (int)r, scaling, st);
 }
 
 extern "C" int bw_lora_merge(const void* w, int64_t ldw, const void* a, const void* b, float scaling, void* w_out,
@@ -971,7 +1214,7 @@ extern "C" int bw_lora_merge(const void* w, int64_t ldw, const void* a, const vo
     return s;
   if (int s = make_tmap_2d(&to, w_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n, k, ldo * 2, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
-  return launch_lora_tc<kModeMerge>(tb, ta, tw, to, (int)n, (int)k, (int)r, scaling, st);
+  return launch_lora_stream<kModeMerge>(tb, ta, tw, to, (int)n, (int)k, (int)r, scaling, st);
 }
 
 namespace bw {

@@ -122,12 +122,18 @@ int bw_w8a16_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, const int8_t*
  * into every rank's Y over peer memory (plain stores), so every rank ends with
  * the whole Y.  y_ranks / signal_ranks are host arrays of `world` device
  * pointers valid in this process (e.g. a symmetric-memory buffer's peer
- * addresses); each signal pad holds >= 2*world + 2 u32 words, zero before the
- * first call, and is not shared with other users.  Every rank must make the same
- * calls in the same order, each with n >= 1; the ranks wait for one another
- * inside the kernel with bounded waits (a timeout shows in bw_device_status).
- * Workspace as bw_w8a16_gemm(m, n, k).  x and w must be TMA-addressable.
+ * addresses); each signal pad holds 2048 u32 words, zero before the first
+ * call, and is not shared with other users.  Every rank must make the same
+ * calls in the same order with the same m, n, k (pad the last rank's shard to
+ * the others' row count), on GPUs with the same SM count: CTA b of every rank
+ * pairs with CTA b of the others;
+ * the ranks wait for one another inside the kernel with bounded waits (a
+ * timeout shows in bw_device_status; the pads must then be zeroed on every
+ * rank before the next call).  Workspace: bw_w8a16_gemm_allgather_workspace_size
+ * bytes, first bw_w8a16_gemm_workspace_zeroed_bytes zero, as for bw_w8a16_gemm.
+ * x and w must be TMA-addressable.
  */
+size_t bw_w8a16_gemm_allgather_workspace_size(int64_t m, int64_t n, int64_t k);
 int bw_w8a16_gemm_allgather(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
                             const void* scale, int scale_dtype, void* const* y_ranks, int64_t ldy,
                             int64_t col0, int64_t m, int64_t n, int64_t k, void* const* signal_ranks,
@@ -196,6 +202,34 @@ typedef struct bw_lora_requant_problem {
 size_t bw_lora_merge_requant_batched_workspace_size(const bw_lora_requant_problem* problems, int count);
 int bw_lora_merge_requant_batched(const bw_lora_requant_problem* problems, int count, void* workspace,
                                   size_t workspace_bytes, void* stream);
+
+/*
+ * Residual + RMSNorm (the W8A16 GEMM's prologue, also callable alone).
+ * Replaces fused_residual_rmsnorm / rmsnorm, src/blackwell_ops/cuda/basic_ops.cu:16-78
+ * (bound at cuda/__init__.py:60-67):
+ *   v = fp32(x[m,:]) + fp32(residual[m,:])   (residual == NULL: v = fp32(x[m,:]))
+ *   out[m,k] = dt(v[k] * rstd * fp32(w[k])),  rstd = 1 / sqrt(sum(v^2) / K + eps)
+ * with the reference kernel's summation order (256 strided partial sums, then a
+ * halving tree) in IEEE fp32.  x, residual: [m, k] dtype (F16 | BF16), row stride
+ * ldx; w: [k]; out: [m, k], row stride ldo.
+ */
+int bw_residual_rmsnorm(const void* x, const void* residual, int dtype, int64_t ldx, const void* w,
+                        float eps, void* out, int64_t ldo, int64_t m, int64_t k, void* stream);
+
+/*
+ * W8A16 GEMM with the residual + RMSNorm prologue, one call:
+ *   y = int8_gemm(fused_residual_rmsnorm(x, residual, norm_w, eps), w, scale)
+ * (reference: basic_ops.cu:49-78 followed by int8_gemm.py:71-107).  The normalised rows are
+ * written to the workspace (bw_w8a16_gemm_rmsnorm_workspace_size bytes, 256-byte aligned, the
+ * first bw_w8a16_gemm_workspace_zeroed_bytes zero) and the GEMM follows with programmatic
+ * dependent launch, so its weight stream overlaps the normalisation.  Results are bit-identical
+ * to bw_residual_rmsnorm followed by bw_w8a16_gemm.
+ */
+size_t bw_w8a16_gemm_rmsnorm_workspace_size(int64_t m, int64_t n, int64_t k);
+int bw_w8a16_gemm_rmsnorm(const void* x, const void* residual, int x_dtype, int64_t ldx, const void* norm_w,
+                          float eps, const int8_t* w, int64_t ldw, const void* scale, int scale_dtype, void* y,
+                          int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                          void* stream);
 
 /*
  * Per-channel int8 quantisation of a KV-cache tensor (the quantiser family's

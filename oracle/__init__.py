@@ -19,6 +19,8 @@ Modules
                ``src/blackwell_ops/cuda/lora_tiled.cu``).
 ``kv``         the KV-cache per-channel quantiser and dequantiser
                (reference ``src/blackwell_ops/cuda/kv_quant.cu:17-58``).
+``norm``       residual + RMSNorm in the reference kernel's summation order
+               (reference ``src/blackwell_ops/cuda/basic_ops.cu:16-78``).
 ``inputs``     seeded synthetic inputs shared by the golden-vector script,
                the tests and the benchmarks.
 ``torch_port`` the reference's CPU PyTorch expressions, verbatim in meaning,

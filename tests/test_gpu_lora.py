@@ -57,7 +57,9 @@ def make(seed, r, n, k):
 CASES = [(c[1], c[2], c[3], c[4], c[5]) for c in LORA_CASES] + [
     (400 + i, r, n, k, 2.0) for i, (r, (_, k, n)) in enumerate((r, p) for r in (16, 128) for p in QWEN)
 ] + [(450, 8, 128, 64, 2.0), (451, 64, 130, 136, 1.0), (452, 32, 1, 128, 2.0), (453, 16, 257, 1000, 2.0),
-      (454, 12, 50, 100, 2.0), (455, 16, 33, 100, 0.75)]  # last two: CUDA-core fallback layouts
+      (454, 12, 50, 100, 2.0), (455, 16, 33, 100, 0.75),  # these two: CUDA-core fallback layouts
+      # several tiles per CTA of the persistent kernel, crossing row blocks; a ragged last column tile
+      (460, 128, 1024, 8192, 2.0), (461, 16, 2000, 4112, 2.0), (462, 64, 640, 3008, 2.0)]
 
 
 @pytest.mark.parametrize("seed,r,n,k,s", CASES)

@@ -43,8 +43,8 @@ def test_gather_peer_that_never_arrives_raises(cuda_dev):
     q = torch.randint(-127, 128, (n, k), generator=g, device=cuda_dev, dtype=torch.int8)
     s = (torch.rand(n, generator=g, device=cuda_dev) * 1e-3 + 1e-4).half()
     ys = [torch.zeros(m, 2 * n, dtype=torch.float16, device=cuda_dev) for _ in range(2)]
-    sigs = [torch.zeros(64, dtype=torch.int32, device=cuda_dev) for _ in range(2)]
-    need = lib.bw_w8a16_gemm_workspace_size(m, n, k)
+    sigs = [torch.zeros(_lib.GATHER_PAD_WORDS, dtype=torch.int32, device=cuda_dev) for _ in range(2)]
+    need = lib.bw_w8a16_gemm_allgather_workspace_size(m, n, k)
     ws = torch.zeros(max(need, 16), dtype=torch.uint8, device=cuda_dev)
     yp = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in ys])
     sp = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in sigs])

@@ -93,7 +93,7 @@ def _worker(rank, world, port, cases, out_dir):
         # here, outside any capture, so the buffer is never freed while a stream is capturing
         del gr, yg
         try:
-            assert fused.fused == ((world - 1) * -(-n // world) < n), "fused path not taken"
+            assert fused.fused, "fused path not taken"
             for i, yf in enumerate(outs):
                 bound = 1e-2 + 2.0 ** (-10 if dt == "f16" else -7) * y.float().abs()
                 d = (yf.float() - y.float()).abs()
