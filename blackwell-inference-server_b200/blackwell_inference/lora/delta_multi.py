@@ -249,6 +249,16 @@ class MultiDeltaLoRAModel:
         with torch.no_grad():
             return self.base(*args, **kwargs)
 
+    def generate_ids(self, input_ids: torch.Tensor, adapter: str | None = None, max_new_tokens: int = 64,
+                     **kwargs) -> torch.Tensor:
+        """Greedy decode from token ids (no tokenizer needed): the new tokens, [batch, <= max_new_tokens]."""
+        self._apply_delta(adapter)
+        input_ids = input_ids.to(self.device)
+        with torch.no_grad():
+            out = self.base.generate(input_ids=input_ids, attention_mask=torch.ones_like(input_ids),
+                                     max_new_tokens=max_new_tokens, do_sample=False, **kwargs)
+        return out[:, input_ids.shape[1]:]
+
     # ---- generation (reference :78-89) ----
     def generate(self, prompt: str, adapter: str | None = None, max_new_tokens: int = 64) -> str:
         if self.tokenizer is None:

@@ -22,7 +22,7 @@ BW_ERR_CUDA = 3
 BW_ERR_DEVICE_TIMEOUT = 4
 BW_ERR_UNSUPPORTED = 5
 
-GATHER_PAD_WORDS = 2048  # u32 words of an all-gather signal pad (include/bw_ops.h)
+GATHER_MAX_M = 256  # largest m of the fused all-gather GEMM (include/bw_ops.h)
 
 DTYPE_CODE = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 
@@ -55,9 +55,10 @@ SIGNATURES = {
     "bw_w8a16_gemm_noalloc": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
                                          _P]),
     "bw_w8a16_gemm_allgather_workspace_size": (_c.c_size_t, [_I64, _I64, _I64]),
-    "bw_w8a16_gemm_allgather": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _c.POINTER(_c.c_void_p),
-                                           _I64, _I64, _I64, _I64, _I64, _c.POINTER(_c.c_void_p), _c.c_int,
-                                           _c.c_int, _P, _c.c_size_t, _P]),
+    "bw_w8a16_gemm_allgather_signal_bytes": (_c.c_size_t, [_I64, _I64, _c.c_int]),
+    "bw_w8a16_gemm_allgather": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
+                                           _I64, _c.POINTER(_c.c_void_p), _c.c_size_t, _c.c_int, _c.c_int, _P,
+                                           _c.c_size_t, _P]),
     "bw_lora_delta": (_c.c_int, [_P, _P, _P, _I64, _I64, _I64, _c.c_float, _P]),
     "bw_add_delta": (_c.c_int, [_P, _P, _I64, _P]),
     "bw_lora_merge": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),

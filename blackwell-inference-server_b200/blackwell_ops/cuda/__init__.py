@@ -82,19 +82,28 @@ def lora_delta_tiled(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0) -> 
 
 
 def add_delta_(W: torch.Tensor, delta: torch.Tensor) -> None:
-    """W += delta, in-place (fp16(fp32 W + fp32 delta))."""
+    """W += delta, in-place (fp16(fp32 W + fp32 delta)), element i of W with element i of delta
+    in logical (row-major) order.
+
+    The reference's checks (lora_ops.cu:62-66: CUDA, fp16, equal numel) are the only ones.  A
+    non-contiguous W is updated through a contiguous copy written back into the view (the
+    reference kernel walks W's storage from its first element instead, which for a strided view
+    pairs the wrong elements and writes outside the view).
+    """
     if not (W.is_cuda and delta.is_cuda):
         raise RuntimeError("W and delta must be CUDA")
     if W.dtype != torch.float16 or delta.dtype != torch.float16:
         raise RuntimeError("must be fp16")
     if W.numel() != delta.numel():
         raise RuntimeError("shape mismatch")
-    if not W.is_contiguous():
-        raise RuntimeError("add_delta_: W must be contiguous")
+    if not W.numel():
+        return
     delta = delta.contiguous()
-    if W.numel():
-        with torch.cuda.device(W.device):
-            check(lib.bw_add_delta(W.data_ptr(), delta.data_ptr(), W.numel(), stream_ptr(W.device)), "add_delta_")
+    target = W if W.is_contiguous() else W.contiguous()
+    with torch.cuda.device(W.device):
+        check(lib.bw_add_delta(target.data_ptr(), delta.data_ptr(), W.numel(), stream_ptr(W.device)), "add_delta_")
+    if target is not W:
+        W.copy_(target)
 
 
 def _check_w(W: torch.Tensor, N: int, K: int) -> torch.Tensor:

@@ -18,16 +18,16 @@ on CPU ranks (gloo) with any function of the same signature; the default is
 the tcgen05 kernel.
 
 ``fused=True`` replaces GEMM + NCCL all-gather by one kernel per rank
-(``bw_w8a16_gemm_allgather``): the epilogue stores every output tile into
-every rank's output buffer over peer memory (a symmetric-memory buffer, plain
-16-byte stores over NVLink) and the ranks exchange bounded completion flags.
-It needs CUDA ranks on one node and at least one output column per rank;
-otherwise the NCCL path runs.  The fused call returns a view of the layer's
-symmetric output buffer, which the layer's next call overwrites (pass ``out=``
-for a copy).  ``check=True`` synchronises after each call and raises
-``DeviceTimeoutError`` if a peer flag wait ran out (a rank that did not make
-the same call); the layer's signal pads must then be reset with ``reset()``
-on every rank before its next call.
+(``bw_w8a16_gemm_allgather``) for M <= 256: each rank's epilogue stores its
+output tiles into its own [M, N] output and sends them to every peer's
+signal-pad mailbox (a symmetric-memory buffer, plain stores over NVLink of
+8-byte words that carry the call's epoch, so no fence or flag handshake is
+needed); each rank copies its peers' tiles into its output as they arrive.  It
+needs CUDA ranks on one node and at least one output column per rank;
+otherwise, and for M > 256, the NCCL path runs.  ``check=True`` synchronises
+after each call and raises ``DeviceTimeoutError`` if a wait for a peer ran out
+(a rank that did not make the same call); the layer's signal pads must then be
+reset with ``reset()`` on every rank before its next call.
 """
 from __future__ import annotations
 
@@ -107,34 +107,31 @@ class ColumnParallelW8A16:
             dist.all_gather(list(buf.unbind(0)), y_local, group=self.group)
         return buf.permute(1, 0, 2).reshape(m, self.world * self.per)[:, : self.n_total]
 
-    def _fused_buffers(self, m: int, dtype: torch.dtype, device: torch.device):
-        """Symmetric output buffer [M, G*Ns] and signal pads for this M (a collective on first use)."""
-        key = (m, dtype)
-        st = self._symm.get(key)
+    def _signal_pads(self, m: int, device: torch.device):
+        """Symmetric signal pads for calls with this M (a collective on first use)."""
+        st = self._symm.get(m)
         if st is None:
             import torch.distributed._symmetric_memory as symm_mem
+
+            from ._lib import lib
 
             group = self.group if self.group is not None else dist.group.WORLD
             enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
             if enable is not None:
                 enable(group.group_name)
-            y = symm_mem.empty((m, self.world * self.per), dtype=dtype, device=device)
-            hy = symm_mem.rendezvous(y, group.group_name)
-            from ._lib import GATHER_PAD_WORDS
-
-            sig = symm_mem.empty((GATHER_PAD_WORDS,), dtype=torch.int32, device=device)
+            nbytes = lib.bw_w8a16_gemm_allgather_signal_bytes(m, self.per, self.world)
+            sig = symm_mem.empty(((nbytes + 15) // 16 * 4,), dtype=torch.int32, device=device)
             sig.zero_()
             hs = symm_mem.rendezvous(sig, group.group_name)
             torch.cuda.synchronize(device)
-            dist.barrier(group=group)  # every rank's flags are zero before anyone signals
-            yp = (ctypes.c_void_p * self.world)(*[int(p) for p in hy.buffer_ptrs])
+            dist.barrier(group=group)  # every rank's pad is zero before anyone sends
             sp = (ctypes.c_void_p * self.world)(*[int(p) for p in hs.buffer_ptrs])
-            st = self._symm[key] = (y, hy, sig, hs, yp, sp)
+            st = self._symm[m] = (sig, hs, sp, sig.numel() * 4)
         return st
 
     def fused_forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """One kernel per rank: local GEMM with the all-gather over peer memory in its epilogue."""
-        from ._lib import DTYPE_CODE, check, lib, stream_ptr
+        from ._lib import DTYPE_CODE, GATHER_MAX_M, check, lib, stream_ptr
         from .kernels.int8_gemm import _workspace
 
         if x.dim() != 2 or x.dtype not in (torch.float16, torch.bfloat16):
@@ -142,22 +139,36 @@ class ColumnParallelW8A16:
         if x.stride(1) != 1:
             x = x.contiguous()
         m, k = x.shape
+        if m > GATHER_MAX_M or m == 0:
+            y = self.gather(self.local(x))
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
         # every rank computes its whole padded shard (per rows; the rows past N are zero weights
-        # whose outputs land in the buffer's padding columns), so all ranks run the same plan
-        y, _, _, _, yp, sp = self._fused_buffers(m, x.dtype, x.device)
+        # whose outputs land in the padding columns), so all ranks run the same plan
+        _, _, sp, nbytes = self._signal_pads(m, x.device)
+        ld = self.world * self.per
+        if out is not None and out.shape == (m, self.n_total) and out.dtype == x.dtype and out.stride() == (ld, 1):
+            y, ret = out, out
+        else:
+            y = torch.empty((m, ld), dtype=x.dtype, device=x.device)
+            ret = None
         st = stream_ptr(x.device)
         need = lib.bw_w8a16_gemm_allgather_workspace_size(m, self.per, k)
         ws = _workspace(x.device, st, need)
         with torch.cuda.device(x.device):
             check(lib.bw_w8a16_gemm_allgather(
                 x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0), self.w.data_ptr(), self.w.stride(0),
-                self.scale.data_ptr(), DTYPE_CODE[self.scale.dtype], yp, self.world * self.per, self.rank * self.per,
-                m, self.per, k, sp, self.world, self.rank, ws.data_ptr() if ws is not None else None,
+                self.scale.data_ptr(), DTYPE_CODE[self.scale.dtype], y.data_ptr(), ld, self.rank * self.per,
+                m, self.per, k, sp, nbytes, self.world, self.rank, ws.data_ptr() if ws is not None else None,
                 ws.numel() if ws is not None else 0, st), "int8_gemm (all-gather)")
         if self.check:
             from .device import check
 
             check(x.device, "int8_gemm (all-gather)")
+        if ret is not None:
+            return ret
         if out is not None:
             out.copy_(y[:, : self.n_total])
             return out
@@ -168,7 +179,7 @@ class ColumnParallelW8A16:
         if not self._symm:
             return
         group = self.group if self.group is not None else dist.group.WORLD
-        for (_, _, sig, _, _, _) in self._symm.values():
+        for (sig, _, _, _) in self._symm.values():
             sig.zero_()
         torch.cuda.synchronize()
         dist.barrier(group=group)

@@ -46,67 +46,54 @@ __device__ __forceinline__ void store_out(void* y, int64_t idx, float v) {
   else static_cast<__half*>(y)[idx] = __float2half_rn(v);
 }
 
-// Column-parallel N-split with the all-gather fused into the epilogue: every
-// output element is stored into every rank's Y (peer memory over NVLink, plain
-// stores), guarded by two flag handshakes on the ranks' signal pads.
+// Column-parallel N-split with the all-gather fused into the epilogue.  Rank p's
+// output columns are [base0 + p*n, base0 + (p+1)*n) of every rank's Y.  A CTA
+// stores the outputs it produces into its own rank's Y and, for every peer, into
+// that peer's mailbox as 8-byte words {2 outputs, call epoch} (plain peer stores
+// over NVLink, no fence: a word is read whole, so its epoch says its data has
+// arrived).  Each rank copies its peers' words into its Y as they arrive.
 struct GatherArgs {
-  unsigned long long y[8];    // each rank's Y [M, ldy]; this rank's columns start at col0
-  unsigned long long sig[8];  // each rank's signal pad (u32, kGatherPadWords): [0,G) ready flags, [G] CTA
-                              // ticket, [G+1] epoch of the last call, [kGatherDone0 + b*8 + p] CTA b of rank
-                              // p has stored its outputs (all zero before the first call)
-  long long col0;
-  int world, rank;            // world == 0: a plain GEMM into y
-  int vec;                    // 1: every Y base is 16-byte aligned and ldy, col0 are multiples of 8
+  unsigned long long ybase;    // this rank's Y at rank 0's first column (rank p's columns: ybase + p*n)
+  unsigned long long pad[8];   // each rank's signal pad: u32 [0] CTA ticket, [1] epoch of the last call
+                               // (zero before the first call); u64 mailbox from byte kMailbox0:
+                               // [epoch parity][source rank][M][rowwords] words {data, epoch}
+  int n;                       // columns per rank
+  int rowwords;                // mailbox words per token row (ceil(n / 128) * 64)
+  int world, rank;             // world == 0: a plain GEMM into y
+  int vec;                     // plain GEMM: Y base 16-byte aligned, ldy and the tile columns multiples of 8
+  int vec4;                    // gather: ybase 8-byte aligned, ldy and n multiples of 4
 };
 
-constexpr int kGatherDone0 = 64;      // first per-CTA done flag of a signal pad
-constexpr int kGatherPadWords = 2048;  // u32 words of a signal pad: room for 248 CTAs x 8 ranks
+constexpr int kMailbox0 = 256;    // byte offset of the mailbox in a signal pad
+constexpr int kGatherMaxM = 256;  // largest M of the fused all-gather (the mailbox grows with M)
 
-// 8 consecutive outputs of one token row, already rounded, as one 16-byte store per rank.
-__device__ __forceinline__ void store_y8(const GatherArgs& g, void* y, int64_t idx, const uint4& v) {
-  if (g.world == 0) {
-    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(y) + idx) = v;
-  } else {
-    for (int r = 0; r < g.world; ++r)
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(g.y[r]) + g.col0 + idx) = v;
-  }
+__host__ __device__ inline size_t gather_pad_bytes(long long m, long long n, int world) {
+  const long long rowwords = (n + 127) / 128 * 64;
+  return kMailbox0 + static_cast<size_t>(2) * world * m * rowwords * 8;
 }
 
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// 8 consecutive outputs of one token row, already rounded, as one 16-byte store.
+__device__ __forceinline__ void store_y8(void* y, int64_t idx, const uint4& v) {
+  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(y) + idx) = v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+
+__device__ __forceinline__ void st_ll2(uint64_t* p, uint32_t a, uint32_t b, uint32_t ep) {
+  const unsigned long long wa = (static_cast<unsigned long long>(ep) << 32) | a;
+  const unsigned long long wb = (static_cast<unsigned long long>(ep) << 32) | b;
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(wa), "l"(wb) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ void ld_ll2(const uint64_t* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
-}
-// Bounded wait until every word of flags[0, n) equals v; false (and the site recorded) on timeout.
-__device__ __forceinline__ bool wait_flags(const uint32_t* flags, int n, uint32_t v, int site) {
-  const long long limit = wait_limit_cycles();
-  const long long t0 = clock64();
-  for (int p = 0; p < n; ++p) {
-    while (ld_acquire_sys(flags + p) != v) {
-      if (clock64() - t0 > limit) {
-        record_timeout(site);
-        return false;
-      }
-    }
-  }
-  return true;
 }
 
 template <bool BF16>
-__device__ __forceinline__ void store_y(void* y, const GatherArgs& g, int64_t ldy, int m, int n, float v) {
-  if (g.world == 0) {
-    store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, v);
-  } else {
-    const int64_t idx = static_cast<int64_t>(m) * ldy + g.col0 + n;
-    for (int r = 0; r < g.world; ++r) store_out<BF16>(reinterpret_cast<void*>(g.y[r]), idx, v);
-  }
+__device__ __forceinline__ void store_y(void* y, int64_t ldy, int m, int n, float v) {
+  store_out<BF16>(y, static_cast<int64_t>(m) * ldy + n, v);
 }
 
 // dt(v): the value an unfused int8_gemm would have written.
@@ -295,8 +282,7 @@ enum PersistentWaitSite : int {
   kSitePEpi = 117,
   kSitePDrain = 118,
   kSitePFinal = 119,
-  kSiteGReady = 130,
-  kSiteGDone = 131,
+  kSiteGRecv = 131,
 };
 
 // GLU = true: the fused gate/up + SwiGLU variant.  A tile is 64 rows of the gate
@@ -335,6 +321,7 @@ __global__ void __launch_bounds__(512, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + XSTAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket = abort_flag + 1;
+  volatile uint32_t* sh_epoch = reinterpret_cast<volatile uint32_t*>(tmem_slot + 3);
   unsigned long long** trace_slot = reinterpret_cast<unsigned long long**>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5;
@@ -597,28 +584,23 @@ __global__ void __launch_bounds__(512, 1)
     float* xch = reinterpret_cast<float*>(smem + C::OFF_XCH);
     pdl_wait();
     if (warp == 10 && lane == 0) trace_stamp(trec, 7);
-    bool gather_ok = true;
     uint32_t epoch = 0;
     if (g.world > 0) {
-      // this call's epoch: one past the last completed call (kept on the device, so a captured
-      // graph replays correctly); ready handshake: this rank's Y may be overwritten now (its
-      // earlier readers are done), and no store goes to a peer before that peer has said the same
+      // this call's epoch: one past the last completed call's (kept on the device, so a captured
+      // graph replays correctly); the last CTA to read it stores it for the next call, which reads
+      // it after this grid has completed, and resets the ticket
       if (warp == 10 && lane == 0) {
-        uint32_t* mine = reinterpret_cast<uint32_t*>(g.sig[g.rank]);
-        epoch = ld_acquire_sys(mine + g.world + 1) + 1u;
-        // the last CTA to read the epoch stores it as this call's (the next call reads it after
-        // this grid has completed) and resets the ticket
-        if (atomicAdd(mine + g.world, 1u) == gridDim.x - 1) {
-          atomicExch(mine + g.world, 0u);
-          atomicExch(mine + g.world + 1, epoch);
+        uint32_t* mine = reinterpret_cast<uint32_t*>(g.pad[g.rank]);
+        const uint32_t e = ld_relaxed_gpu(mine + 1) + 1u;
+        if (atomicAdd(mine, 1u) == gridDim.x - 1) {
+          atomicExch(mine, 0u);
+          atomicExch(mine + 1, e);
         }
-        if (blockIdx.x == 0)
-          for (int p = 0; p < g.world; ++p) st_release_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + g.rank, epoch);
-        gather_ok = wait_flags(mine, g.world, epoch, kSiteGReady);
-        if (!gather_ok) *abort_flag = 1;
+        *sh_epoch = e;
         trace_stamp(trec, 5);
       }
-      gather_ok = !named_bar_any(1, 128, !gather_ok);
+      named_bar_sync(1, 128);
+      epoch = *sh_epoch;
     }
     int j = 0;
     int it0 = 0;  // this CTA's k-block count before the segment
@@ -659,10 +641,11 @@ __global__ void __launch_bounds__(512, 1)
       auto emit = [&](const float* v, int c0, auto ch_tag) {
         constexpr int CH = decltype(ch_tag)::value;
         if constexpr (!GLU) {
-          if (g.vec) {
+          if (g.vec || g.world > 0) {
             // Stage the CH x 128 outputs of the chunk as dt values in shared memory (token-major),
-            // then store 16-byte rows of 8 outputs: one vector store per rank per 8 outputs instead
-            // of eight 2-byte stores.  Outputs past N (last tile) are stored element by element.
+            // then store 16-byte rows of 8 outputs: one vector store per 8 outputs instead of eight
+            // 2-byte stores (outputs past N or a misaligned Y: element by element).  All-gather:
+            // the same 8 outputs go to every peer's mailbox as four {2 outputs, epoch} words.
             uint16_t* st = reinterpret_cast<uint16_t*>(xch);
 #pragma unroll
             for (int e = 0; e < CH; ++e) {
@@ -677,16 +660,22 @@ __global__ void __launch_bounds__(512, 1)
               const int m = m0 + c0 + e;
               if (m < M) {
                 const uint4 val = *reinterpret_cast<const uint4*>(st + e * 128 + c8);
+                if (g.world > 0) {
+                  const size_t off = (static_cast<size_t>((epoch & 1u) * g.world + g.rank) * M + m) * g.rowwords +
+                                     ((n0 + c8) >> 1);
+                  for (int r = 0; r < g.world; ++r) {
+                    if (r == g.rank) continue;
+                    uint64_t* mb = reinterpret_cast<uint64_t*>(g.pad[r] + kMailbox0) + off;
+                    st_ll2(mb, val.x, val.y, epoch);
+                    st_ll2(mb + 2, val.z, val.w, epoch);
+                  }
+                }
                 const int64_t idx = static_cast<int64_t>(m) * ldy + n0 + c8;
-                if (n0 + c8 + 8 <= N) {
-                  store_y8(g, y, idx, val);
+                if (g.vec && n0 + c8 + 8 <= N) {
+                  store_y8(y, idx, val);
                 } else {
                   const uint16_t* h = reinterpret_cast<const uint16_t*>(&val);
-                  for (int q8 = 0; q8 < 8 && n0 + c8 + q8 < N; ++q8) {
-                    if (g.world == 0) static_cast<uint16_t*>(y)[idx + q8] = h[q8];
-                    else
-                      for (int r = 0; r < g.world; ++r) reinterpret_cast<uint16_t*>(g.y[r])[g.col0 + idx + q8] = h[q8];
-                  }
+                  for (int q8 = 0; q8 < 8 && n0 + c8 + q8 < N; ++q8) static_cast<uint16_t*>(y)[idx + q8] = h[q8];
                 }
               }
             }
@@ -695,7 +684,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
             for (int e = 0; e < CH; ++e) {
               const int m = m0 + c0 + e;
-              if (m < M) store_y<BF16>(y, g, ldy, m, n, v[e]);
+              if (m < M) store_y<BF16>(y, ldy, m, n, v[e]);
             }
           }
         } else {
@@ -710,7 +699,7 @@ __global__ void __launch_bounds__(512, 1)
               const int m = m0 + c0 + e;
               const float gt = round_out<BF16>(v[e]);
               const float up = xch[row * 16 + e];
-              if (m < M) store_y<BF16>(y, g, ldy, m, n, gt / (1.0f + expf(-gt)) * up);
+              if (m < M) store_y<BF16>(y, ldy, m, n, gt / (1.0f + expf(-gt)) * up);
             }
           }
           named_bar_sync(1, 128);  // the buffer is read before the next chunk overwrites it
@@ -812,25 +801,67 @@ __global__ void __launch_bounds__(512, 1)
       }
     }
     if (warp == 10 && lane == 0) trace_stamp(trec, 3);
-    if (g.world > 0) {
-      // done handshake: the last CTA of this rank tells every peer that this rank's columns
-      // are in its Y, then waits until every peer has said the same (bounded)
-      // Completion, CTA by CTA: CTA b of this rank tells CTA b of every rank that its outputs are
-      // stored, then waits for the same word from CTA b of every peer (every rank runs the same
-      // grid), so when every CTA of a rank is past its wait, every peer's outputs are in its Y.
-      // Memory order: the CTA's stores -> bar.sync -> a system-scope fence by the flag thread
-      // (cumulative over the stores the barrier made it observe) -> the flags; readers acquire.
-      // The fences of the CTAs run side by side as each CTA finishes, not at the end of the call.
-      named_bar_sync(1, 128);
-      if (warp == 10 && lane == 0) {
-        fence_acq_rel_sys();
-        for (int p = 0; p < g.world; ++p)
-          st_relaxed_sys(reinterpret_cast<uint32_t*>(g.sig[p]) + kGatherDone0 + blockIdx.x * 8 + g.rank, epoch);
-        trace_stamp(trec, 4);
-        const uint32_t* mine = reinterpret_cast<const uint32_t*>(g.sig[g.rank]);
-        if (gather_ok && !*abort_flag) wait_flags(mine + kGatherDone0 + blockIdx.x * 8, g.world, epoch, kSiteGDone);
-        trace_stamp(trec, 6);
+    // (all four warps decide together: a barrier inside must see all of them)
+    if (g.world > 0 && !named_bar_any(1, 128, *abort_flag != 0)) {
+      // Receive: the (tile, peer) pairs are dealt to the CTAs round robin (the same on every rank;
+      // which peer CTA produced a tile does not matter).  A thread polls 8 words (16 outputs) at a
+      // time, the loads issued together; a word belongs to this call when its epoch does, and
+      // stale words (an older call of this parity) never do.  Bounded: a peer that never sends
+      // records the site and stops this CTA's receive.
+      const int peers = g.world - 1;
+      const int tiles = sc.m_tiles * sc.n_tiles;
+      const uint64_t* mbox = reinterpret_cast<const uint64_t*>(g.pad[g.rank] + kMailbox0);
+      const long long limit = wait_limit_cycles();
+      const long long tw0 = clock64();
+      bool ok = true;
+      for (int q = blockIdx.x; ok && q < tiles * peers; q += gridDim.x) {
+        const int t = q / peers;
+        const int p = q - t * peers + (q - t * peers >= g.rank ? 1 : 0);
+        const int nt = t / sc.m_tiles, mt = t - nt * sc.m_tiles;
+        const int rows = min(BM, M - mt * BM);
+        const uint64_t* src =
+            mbox + (static_cast<size_t>((epoch & 1u) * g.world + p) * M + mt * BM) * g.rowwords + nt * 64;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(g.ybase) + static_cast<int64_t>(mt * BM) * ldy +
+                        static_cast<int64_t>(p) * g.n + nt * 128;
+        const int cols = min(128, g.n - nt * 128);
+        for (int w0 = row * 2; ok && w0 < rows * 64; w0 += 4 * 256) {
+          unsigned long long v[4][2];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int w = w0 + i * 256;
+            if (w < rows * 64) ld_ll2(src + static_cast<size_t>(w >> 6) * g.rowwords + (w & 63), v[i][0], v[i][1]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int w = w0 + i * 256;
+            if (w >= rows * 64) break;
+            const uint64_t* a = src + static_cast<size_t>(w >> 6) * g.rowwords + (w & 63);
+            while (static_cast<uint32_t>(v[i][0] >> 32) != epoch || static_cast<uint32_t>(v[i][1] >> 32) != epoch) {
+              if (clock64() - tw0 > limit) {
+                record_timeout(kSiteGRecv);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+              ld_ll2(a, v[i][0], v[i][1]);
+            }
+            if (!ok) break;
+            // 4 outputs: token w / 64, columns 2 (w % 64) .. + 3 of the tile
+            const int c = 2 * (w & 63);
+            uint16_t* d = dst + static_cast<int64_t>(w >> 6) * ldy + c;
+            const uint32_t lo = static_cast<uint32_t>(v[i][0]), hi = static_cast<uint32_t>(v[i][1]);
+            if (g.vec4 && c + 4 <= cols) {
+              *reinterpret_cast<uint2*>(d) = make_uint2(lo, hi);
+            } else {
+              const uint16_t h4[4] = {static_cast<uint16_t>(lo), static_cast<uint16_t>(lo >> 16),
+                                      static_cast<uint16_t>(hi), static_cast<uint16_t>(hi >> 16)};
+              for (int u = 0; u < 4 && c + u < cols; ++u) d[u] = h4[u];
+            }
+          }
+        }
       }
+      named_bar_sync(1, 128);
+      if (warp == 10 && lane == 0) trace_stamp(trec, 6);
     }
   }
 
@@ -1105,7 +1136,7 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
   const GemmPlan p = plan_gemm(m, n, k, glu, g.world > 0);
   if (p.units < 0) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: m=%lld n=%lld is too many output tiles",
                                (long long)m, (long long)n);
-  if (g.world > 0 && (p.mode != 1 || p.grid > (kGatherPadWords - kGatherDone0) / 8))
+  if (g.world > 0 && p.mode != 1)
     return fail(BW_ERR_UNSUPPORTED, "int8_gemm (all-gather): shape m=%lld n=%lld k=%lld has no stream-K plan",
                 (long long)m, (long long)n, (long long)k);
   float* ws = nullptr;
@@ -1175,35 +1206,50 @@ extern "C" int bw_w8a16_gemm_swiglu(const void* x, int x_dtype, int64_t ldx, con
 }
 
 // Column-parallel N-split GEMM with the all-gather in the epilogue: this rank's output columns
-// [col0, col0 + n) are stored into every rank's Y over peer memory, then the ranks exchange
-// completion flags (bounded waits; a timeout shows in bw_device_status).
+// [col0, col0 + n) of y are computed here and sent to every peer's signal-pad mailbox; the peers'
+// columns (rank p: [col0 + (p - rank) n, ... + n)) arrive in this rank's mailbox and are copied
+// into y before the kernel ends.  Waits are bounded; a timeout shows in bw_device_status.
+extern "C" size_t bw_w8a16_gemm_allgather_signal_bytes(int64_t m, int64_t n, int world) {
+  if (m <= 0 || n <= 0 || world < 1 || world > 8) return 0;
+  return bw::gather_pad_bytes(m, n, world);
+}
+
 extern "C" int bw_w8a16_gemm_allgather(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
-                                       const void* scale, int scale_dtype, void* const* y_ranks, int64_t ldy,
-                                       int64_t col0, int64_t m, int64_t n, int64_t k, void* const* signal_ranks,
-                                       int world, int rank, void* workspace, size_t workspace_bytes, void* stream) {
+                                       const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t col0,
+                                       int64_t m, int64_t n, int64_t k, void* const* signal_ranks,
+                                       size_t signal_bytes, int world, int rank, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
   using namespace bw;
   if (world < 1 || world > 8 || rank < 0 || rank >= world)
     return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): need 1 <= world <= 8 and 0 <= rank < world");
-  if (!y_ranks || !signal_ranks) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): null pointer list");
-  if (col0 < 0 || col0 + n > ldy)
-    return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): columns [%lld, %lld) outside the row stride %lld",
-                (long long)col0, (long long)(col0 + n), (long long)ldy);
+  if (!y || !signal_ranks) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): null pointer");
+  if (m < 0 || n < 0 || m > kGatherMaxM)
+    return fail(BW_ERR_UNSUPPORTED, "int8_gemm (all-gather): m = %lld outside [0, %d]", (long long)m, kGatherMaxM);
+  if (n > (1LL << 30) || col0 < rank * n || col0 + (world - rank) * n > ldy)
+    return fail(BW_ERR_INVALID_ARGUMENT,
+                "int8_gemm (all-gather): the %d ranks' columns around [%lld, %lld) do not fit the row stride %lld",
+                world, (long long)col0, (long long)(col0 + n), (long long)ldy);
+  if (m == 0 || n == 0) return BW_OK;
+  if (signal_bytes < gather_pad_bytes(m, n, world))
+    return fail(BW_ERR_WORKSPACE, "int8_gemm (all-gather): signal pads of %zu bytes required, %zu given",
+                gather_pad_bytes(m, n, world), signal_bytes);
   GatherArgs g = {};
   for (int r = 0; r < world; ++r) {
-    if (!y_ranks[r] || !signal_ranks[r])
-      return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): null pointer for rank %d", r);
-    if (reinterpret_cast<uintptr_t>(signal_ranks[r]) % 4 != 0)
-      return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): signal pad of rank %d is not 4-byte aligned", r);
-    g.y[r] = reinterpret_cast<unsigned long long>(y_ranks[r]);
-    g.sig[r] = reinterpret_cast<unsigned long long>(signal_ranks[r]);
+    if (!signal_ranks[r]) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): null signal pad for rank %d", r);
+    if (reinterpret_cast<uintptr_t>(signal_ranks[r]) % 16 != 0)
+      return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm (all-gather): signal pad of rank %d is not 16-byte aligned", r);
+    g.pad[r] = reinterpret_cast<unsigned long long>(signal_ranks[r]);
   }
-  g.col0 = col0;
+  uint16_t* yl = static_cast<uint16_t*>(y) + col0;
+  g.ybase = reinterpret_cast<unsigned long long>(yl - rank * n);
+  g.n = static_cast<int>(n);
+  g.rowwords = static_cast<int>((n + 127) / 128 * 64);
   g.world = world;
   g.rank = rank;
-  g.vec = ldy % 8 == 0 && col0 % 8 == 0;
-  for (int r = 0; r < world; ++r) g.vec &= reinterpret_cast<uintptr_t>(y_ranks[r]) % 16 == 0;
-  return gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y_ranks[rank], ldy, m, n, k, workspace,
-                   workspace_bytes, g, stream);
+  g.vec = reinterpret_cast<uintptr_t>(yl) % 16 == 0 && ldy % 8 == 0;
+  g.vec4 = g.ybase % 8 == 0 && ldy % 4 == 0 && n % 4 == 0;
+  return gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, yl, ldy, m, n, k, workspace, workspace_bytes, g,
+                   stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -117,27 +117,32 @@ int bw_w8a16_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, const int8_t*
 /*
  * Column-parallel N-split W8A16 GEMM with the all-gather fused into the
  * epilogue (the north star's N-split; the reference has no multi-GPU path).
- * Rank `rank` of `world` (<= 8) holds w rows [0, n) of its shard and owns output
- * columns [col0, col0 + n) of Y [m, ldy]; each output tile is stored straight
- * into every rank's Y over peer memory (plain stores), so every rank ends with
- * the whole Y.  y_ranks / signal_ranks are host arrays of `world` device
- * pointers valid in this process (e.g. a symmetric-memory buffer's peer
- * addresses); each signal pad holds 2048 u32 words, zero before the first
- * call, and is not shared with other users.  Every rank must make the same
- * calls in the same order with the same m, n, k (pad the last rank's shard to
- * the others' row count), on GPUs with the same SM count: CTA b of every rank
- * pairs with CTA b of the others;
- * the ranks wait for one another inside the kernel with bounded waits (a
- * timeout shows in bw_device_status; the pads must then be zeroed on every
- * rank before the next call).  Workspace: bw_w8a16_gemm_allgather_workspace_size
- * bytes, first bw_w8a16_gemm_workspace_zeroed_bytes zero, as for bw_w8a16_gemm.
- * x and w must be TMA-addressable.
+ * Rank `rank` of `world` (<= 8) holds w rows [0, n) of its shard; rank p's
+ * output columns are [col0 + (p - rank) n, col0 + (p - rank + 1) n) of y
+ * [m, ldy], a plain device buffer of this rank.  Each output tile this rank
+ * computes is stored into y and, as 8-byte {2 outputs, call epoch} words, into
+ * every peer's signal pad (plain stores over NVLink, no fence); the kernel
+ * copies its peers' words into y as they arrive, so y holds all world * n
+ * columns when the kernel ends.  signal_ranks is a host array of `world`
+ * device pointers valid in this process (e.g. a symmetric-memory buffer's peer
+ * addresses), 16-byte aligned, each pad signal_bytes >=
+ * bw_w8a16_gemm_allgather_signal_bytes(m, n, world) long, zero before the
+ * first call and not shared with other users.  m <= 256.  Every rank must make
+ * the same calls in the same order with the same m, n, k (pad the last rank's
+ * shard to the others' row count), on GPUs with the same SM count: the ranks
+ * share one tile schedule.  Waits for peers are bounded (a timeout shows in
+ * bw_device_status; the pads must then be zeroed on every rank before the
+ * next call).  Workspace: bw_w8a16_gemm_allgather_workspace_size bytes, first
+ * bw_w8a16_gemm_workspace_zeroed_bytes zero, as for bw_w8a16_gemm.  x and w
+ * must be TMA-addressable.
  */
 size_t bw_w8a16_gemm_allgather_workspace_size(int64_t m, int64_t n, int64_t k);
+size_t bw_w8a16_gemm_allgather_signal_bytes(int64_t m, int64_t n, int world);
 int bw_w8a16_gemm_allgather(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
-                            const void* scale, int scale_dtype, void* const* y_ranks, int64_t ldy,
-                            int64_t col0, int64_t m, int64_t n, int64_t k, void* const* signal_ranks,
-                            int world, int rank, void* workspace, size_t workspace_bytes, void* stream);
+                            const void* scale, int scale_dtype, void* y, int64_t ldy, int64_t col0,
+                            int64_t m, int64_t n, int64_t k, void* const* signal_ranks,
+                            size_t signal_bytes, int world, int rank, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /*
  * LoRA delta: delta[n, k] = fp16( fp32(sum_j b[n,j] * a[j,k]) * scaling ).

@@ -194,9 +194,11 @@ def test_gemm_workspace_shared_across_shapes(cuda_dev):
     assert _lib.device_status() == 0
 
 
-@pytest.mark.parametrize("m,n,k", [(2048, 14336, 4096), (512, 4096, 14336), (4096, 8192, 2048)])
+@pytest.mark.parametrize("m,n,k", [(2048, 14336, 4096), (512, 4096, 14336), (4096, 8192, 2048), (8192, 14336, 4096),
+                                   (8192, 4096, 14336)])
 def test_gemm_prefill_full_size_vs_torch_fp32(m, n, k, cuda_dev, ops):
-    """Full prefill sizes: compared with torch's fp32 dequantise-matmul on the GPU (TF32 off)."""
+    """Full prefill sizes (cfg4's Llama-3-8B MLP shapes up to M = 8192): compared with the
+    dequantise-matmul in fp64 on the GPU."""
     g = torch.Generator(device=cuda_dev).manual_seed(m + n)
     w = (torch.randn(n, k, generator=g, device=cuda_dev) * 0.02).to(torch.bfloat16)
     from blackwell_ops.kernels import quantize_weight_int8

@@ -119,6 +119,21 @@ def test_add_delta_bit_exact(cuda_dev, ops):
     want = lora.add_delta(a.cpu().numpy(), b.cpu().numpy())
     cuda.add_delta_(a, b)
     assert np.array_equal(a.cpu().numpy(), want)
+    # a strided W (a column slice and a transposed view) is updated element for element in
+    # logical order, and nothing outside the view changes
+    base = dev16(inputs.weight(3, 96, 130, F16), cuda_dev)
+    keep = base.clone()
+    view = base[:, 2:66]
+    D = dev16(inputs.weight(4, 96, 64, F16), cuda_dev)
+    want = lora.add_delta(view.cpu().numpy(), D.cpu().numpy())
+    cuda.add_delta_(view, D)
+    assert np.array_equal(view.cpu().numpy(), want)
+    assert torch.equal(base[:, :2], keep[:, :2]) and torch.equal(base[:, 66:], keep[:, 66:])
+    wt = dev16(inputs.weight(5, 80, 48, F16), cuda_dev).t()
+    D = dev16(inputs.weight(6, 48, 80, F16), cuda_dev)
+    want = lora.add_delta(wt.cpu().numpy(), D.cpu().numpy())
+    cuda.add_delta_(wt, D)
+    assert np.array_equal(wt.cpu().numpy(), want)
 
 
 def test_lora_errors_match_reference_messages(cuda_dev, ops):

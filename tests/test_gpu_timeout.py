@@ -1,8 +1,8 @@
 """Bounded device waits run out into an error, not a hang (one GPU, no fault).
 
-The fused all-gather GEMM waits for its peers' flags.  Here rank 0 of a
-"world" of two is launched alone: rank 1's signal pad is a local buffer that
-no kernel ever writes, so rank 0's wait for it must run out.  With the wait
+The fused all-gather GEMM waits for its peers' output words in its own
+signal-pad mailbox.  Here rank 0 of a "world" of two is launched alone: no
+rank 1 ever sends, so rank 0's wait must run out.  With the wait
 limit set to 20 ms the kernel returns, the device status records the wait
 site, ``blackwell_ops.device.check`` raises ``DeviceTimeoutError`` (a
 ``RuntimeError``), and the device stays usable: a plain GEMM afterwards still
@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 
-SITE_READY, SITE_DONE = 130, 131
+SITE_RECEIVE = 131  # the wait for a peer's mailbox words
 
 
 def test_wait_limit_roundtrip(cuda_dev):
@@ -42,23 +42,24 @@ def test_gather_peer_that_never_arrives_raises(cuda_dev):
     x = torch.randn(m, k, generator=g, device=cuda_dev).half()
     q = torch.randint(-127, 128, (n, k), generator=g, device=cuda_dev, dtype=torch.int8)
     s = (torch.rand(n, generator=g, device=cuda_dev) * 1e-3 + 1e-4).half()
-    ys = [torch.zeros(m, 2 * n, dtype=torch.float16, device=cuda_dev) for _ in range(2)]
-    sigs = [torch.zeros(_lib.GATHER_PAD_WORDS, dtype=torch.int32, device=cuda_dev) for _ in range(2)]
+    y = torch.zeros(m, 2 * n, dtype=torch.float16, device=cuda_dev)
+    nbytes = lib.bw_w8a16_gemm_allgather_signal_bytes(m, n, 2)
+    sigs = [torch.zeros(nbytes // 4, dtype=torch.int32, device=cuda_dev) for _ in range(2)]
     need = lib.bw_w8a16_gemm_allgather_workspace_size(m, n, k)
     ws = torch.zeros(max(need, 16), dtype=torch.uint8, device=cuda_dev)
-    yp = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in ys])
     sp = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in sigs])
     assert device.status(cuda_dev, clear=True) == 0
     old = device.wait_limit(cuda_dev)
     device.set_wait_limit(0.02, cuda_dev)
     try:
-        rc = lib.bw_w8a16_gemm_allgather(x.data_ptr(), 0, k, q.data_ptr(), k, s.data_ptr(), 0, yp, 2 * n, 0, m, n, k,
-                                         sp, 2, 0, ws.data_ptr(), ws.numel(), _lib.stream_ptr(cuda_dev))
+        rc = lib.bw_w8a16_gemm_allgather(x.data_ptr(), 0, k, q.data_ptr(), k, s.data_ptr(), 0, y.data_ptr(), 2 * n,
+                                         0, m, n, k, sp, nbytes, 2, 0, ws.data_ptr(), ws.numel(),
+                                         _lib.stream_ptr(cuda_dev))
         assert rc == 0, lib.bw_last_error()
         with pytest.raises(device.DeviceTimeoutError) as err:
             device.check(cuda_dev, "int8_gemm (all-gather)")
         assert isinstance(err.value, RuntimeError)
-        assert err.value.site in (SITE_READY, SITE_DONE)
+        assert err.value.site == SITE_RECEIVE
         assert "timed out" in str(err.value)
         assert device.status(cuda_dev) == 0  # check() cleared it
     finally:
