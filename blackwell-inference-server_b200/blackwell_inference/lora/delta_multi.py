@@ -200,6 +200,11 @@ class MultiDeltaLoRAModel:
                     raise RuntimeError("a layer was built without its fp16 base weight; cannot merge adapters")
             outs = lora_merge_requant_batched(
                 (layer.base_weight, used[n][0], used[n][1], used[n][2]) for n, layer in zip(names, layers))
+            # adapter loading is not on the serving path: synchronise and raise if a device wait of
+            # the batched requantisation ran out (its codes would be incomplete)
+            from blackwell_ops.device import check
+
+            check(layers[0].base_weight.device, f"load_adapter({name!r})")
             for layer, (q, s) in zip(layers, outs):
                 layer.copies[name] = (q, s)
         self._adapters[name] = used

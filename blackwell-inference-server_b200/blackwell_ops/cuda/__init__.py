@@ -45,6 +45,13 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
     return ws
 
 
+def reset_workspaces() -> None:
+    """Zero every cached requantisation workspace (needed only after a device-side timeout, which
+    can leave a grid barrier or a set of row maxima mid-way)."""
+    for ws in _ws.values():
+        ws.zero_()
+
+
 def _check_ab(A: torch.Tensor, B: torch.Tensor) -> tuple[int, int, int]:
     if not (A.is_cuda and B.is_cuda):
         raise RuntimeError("A and B must be CUDA")

@@ -57,13 +57,15 @@ def status(device=None, clear: bool = False) -> int:
 def check(device=None, op: str = "blackwell_ops") -> None:
     """Raise ``DeviceTimeoutError`` if a bounded wait of a kernel on ``device`` ran out.
 
-    Clears the status and re-zeroes the cached GEMM workspaces first, so the next
-    call starts clean.  Synchronises the device's current stream."""
+    Clears the status and re-zeroes the cached GEMM and requantisation workspaces first,
+    so the next call starts clean.  Synchronises the device's current stream."""
     site = status(device, clear=True)
     if site:
+        from .cuda import reset_workspaces as reset_requant
         from .kernels.int8_gemm import reset_workspaces
 
         reset_workspaces()
+        reset_requant()
         torch.cuda.synchronize(_dev(device))
         err = DeviceTimeoutError(BW_ERR_DEVICE_TIMEOUT, op)
         err.site = site

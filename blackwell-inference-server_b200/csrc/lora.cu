@@ -39,28 +39,7 @@ namespace bw {
 
 enum LoraMode : int { kModeDelta = 0, kModeMerge = 1 };
 
-enum LoraWaitSite : int {
-  kSiteLoraB = 201,
-  kSiteLoraTile = 202,
-  kSiteLoraMma = 203,
-};
-
 constexpr int kLoraMaxR = 128;
-
-struct LoraSmem {
-  int rp;  // rank rounded up to 16
-  int nbp;  // 64-wide rank panels of the B tile
-  int off_b, off_a, off_w, off_bar, total;
-  __host__ __device__ explicit LoraSmem(int r) {
-    rp = (r + 15) / 16 * 16;
-    nbp = (rp + 63) / 64;
-    off_b = 0;
-    off_a = off_b + nbp * 16384;
-    off_w = off_a + ((2 * rp * 128 + 1023) / 1024) * 1024;
-    off_bar = off_w + 32768;
-    total = off_bar + 128 + 1024;
-  }
-};
 
 __device__ __forceinline__ float h2f_lo(uint32_t w) { return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu))); }
 __device__ __forceinline__ float h2f_hi(uint32_t w) { return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))); }
@@ -102,93 +81,6 @@ __device__ __forceinline__ void lora_tile_epilogue(uint32_t taddr, uint8_t* sW, 
   }
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(128)
-    lora_tc_kernel(const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
-                   const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_out, int N, int K,
-                   int r, float scaling) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const LoraSmem L(r);
-  uint8_t* sB = smem + L.off_b;
-  uint8_t* sA = smem + L.off_a;
-  uint8_t* sW = smem + L.off_w;
-  uint64_t* bar_t = reinterpret_cast<uint64_t*>(smem + L.off_bar);
-  uint64_t* bar_mma = bar_t + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_t + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int row = warp * 32 + lane;  // 128 threads: warp w owns TMEM lanes 32w..32w+31
-  const int n0 = blockIdx.y * 128;
-  const int k0 = blockIdx.x * 128;
-  const int rp = L.rp;
-
-  if (tid == 0) {
-    mbar_init(bar_t, 1);
-    mbar_init(bar_mma, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    // B, A (and W) tiles on one barrier
-    const uint32_t bytes = L.nbp * 16384 + 2 * rp * 128 + (MODE != kModeDelta ? 32768 : 0);
-    mbar_arrive_expect_tx(bar_t, bytes);
-    const uint64_t keep = l2_policy_evict_last();
-    for (int p = 0; p < L.nbp; ++p) tma_load_2d(sB + p * 16384, &tm_b, bar_t, p * 64, n0, keep);
-    tma_load_2d(sA, &tm_a, bar_t, k0, 0, keep);
-    tma_load_2d(sA + rp * 128, &tm_a, bar_t, k0 + 64, 0, keep);
-    if (MODE != kModeDelta) {
-      const uint64_t once = l2_policy_evict_first();
-      tma_load_2d(sW, &tm_w, bar_t, k0, n0, once);
-      tma_load_2d(sW + 16384, &tm_w, bar_t, k0 + 64, n0, once);
-    }
-  }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, 128);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-
-  if (tid == 0) {
-    if (mbar_wait(bar_t, 0, abort_flag, kSiteLoraTile)) {
-      tc_fence_after();
-      const uint32_t idesc = make_idesc_f16(128, 128, false, true);
-      const uint32_t b_base = smem_u32(sB);
-      const uint32_t a_base = smem_u32(sA);
-      for (int kk = 0; kk < rp / 16; ++kk) {
-        const uint64_t ad = make_sdesc(b_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-        const uint64_t bd = make_sdesc(a_base + kk * 2048, rp * 128, 1024, kLayoutSW128);
-        umma_f16(tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
-      }
-    }
-    umma_commit(bar_mma);  // always, so waiters never wait on an op that was not issued
-  }
-  bool ok = mbar_wait(bar_t, 0, abort_flag, kSiteLoraTile) && mbar_wait(bar_mma, 0, abort_flag, kSiteLoraMma);
-  tc_fence_after();
-  ok = !__syncthreads_or(!ok || *abort_flag);  // one decision for the whole CTA
-  if (ok) lora_tile_epilogue<MODE>(taddr, sW, row, scaling);
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  if (tid == 0 && ok) {
-    tma_store_2d(&tm_out, sW, k0, n0);
-    if (k0 + 64 < K) tma_store_2d(&tm_out, sW + 16384, k0 + 64, n0);  // never start a store past K
-    tma_store_commit();
-    tma_store_wait0();
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 128);
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Persistent ΔW / merge: one CTA per SM walks a contiguous range of 128 x 128 output tiles in
 // row-major order, so a CTA keeps the row block's B[128, r] resident across its k-tiles and
@@ -200,7 +92,6 @@ __global__ void __launch_bounds__(128)
 //   warps 4-11  epilogue, two groups of four taking alternate tiles, thread = row: fp16(acc * s)
 //               (delta) or fp16(W + fp16(acc * s)) (merge), staged in the 128-byte-swizzled
 //               layout and written by TMA stores
-// The arithmetic is lora_tile_epilogue's, so the output bits equal lora_tc_kernel's.
 // ---------------------------------------------------------------------------
 struct LoraStreamSmem {
   int rp, nbp, a_bytes, b_bytes, wslots, aslots, off_a, off_b, off_w, off_bar, total;
@@ -973,23 +864,6 @@ __global__ void __launch_bounds__(256) lora_requant_simt_kernel(const __half* __
 static bool lora_tc_ok(const void* a, const void* b, int64_t k, int64_t r) {
   const auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   return al16(a) && al16(b) && r >= 1 && r <= kLoraMaxR && r % 8 == 0 && k % 8 == 0;
-}
-
-template <int MODE>
-static int launch_lora_tc(const CUtensorMap& tb, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to,
-                          int N, int K, int r, float s, cudaStream_t st) {
-  const LoraSmem L(r);
-  static std::once_flag once[64];
-  static cudaError_t err[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::call_once(once[dev & 63], [&] {
-    err[dev & 63] = cudaFuncSetAttribute(lora_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  });
-  if (int rc = check_cuda(err[dev & 63], "cudaFuncSetAttribute(lora_tc_kernel)")) return rc;
-  dim3 grid((K + 127) / 128, (N + 127) / 128);
-  lora_tc_kernel<MODE><<<grid, 128, L.total, st>>>(tb, ta, tw, to, N, K, r, s);
-  return check_launch("lora_tc_kernel");
 }
 
 template <int MODE>
