@@ -15,9 +15,9 @@ without finishing its output.  This module turns that into Python errors:
   spin wait on a device (default 4 s).
 * ``Trace`` records, per CTA of each traced kernel launch, globaltimer stamps of
   its phases (start, first weight tile landed, last MMA complete, epilogue
-  done with every output stored and sent, and for the fused all-gather: call
-  epoch read, every peer's outputs received; and when the preceding kernel
-  completed), so a caller can see which phase bounds a step.
+  done, the deferred stream-K reductions done, and for the fused all-gather:
+  call epoch read, every peer's outputs received; and when the preceding
+  kernel completed), so a caller can see which phase bounds a step.
 """
 from __future__ import annotations
 
@@ -86,7 +86,7 @@ def wait_limit(device=None) -> float:
     return ns.value / 1e9
 
 
-PHASES = ("start", "first_tile", "mma_done", "epilogue_done", "unused", "epoch_read", "gather_done",
+PHASES = ("start", "first_tile", "mma_done", "epilogue_done", "reduce_done", "epoch_read", "gather_done",
           "predecessor_done")
 RECORD_WORDS = 16
 KERNEL_IDS = {1: "w8a16_persistent", 2: "w8a16_persistent_swiglu"}

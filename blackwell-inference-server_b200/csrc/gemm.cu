@@ -143,6 +143,15 @@ __device__ __forceinline__ float round_out(float v) {
 // its own accumulator; BM = 128 one.  A third issuer (warp 15, with the weight producer also
 // loading the activation tiles) measured slower on the Llama-3-70B MLP decode shapes (3.1 against
 // 4.0 TB/s): the single producer then issued one weight tile per ~1250 cycles.
+// Activation ring depth at BM = 16 (the weight ring takes the rest of 208 KB).
+#ifndef BW_GEMM_XSTAGES16
+#define BW_GEMM_XSTAGES16 16
+#endif
+// The weight producer requests this many consecutive k-blocks of the same rows back to back
+// (waiting for that many free slots), so a row's adjacent 128-byte blocks reach DRAM together.
+#ifndef BW_GEMM_W_GROUP
+#define BW_GEMM_W_GROUP 1
+#endif
 #ifndef BW_GEMM_DEC_ISSUERS
 #define BW_GEMM_DEC_ISSUERS 2
 #endif
@@ -167,7 +176,7 @@ struct PCfg {
   // weight tiles already issued, so an activation tile must be issued with (or before) its
   // k-block's weight tile; with a shallow ring its slot frees only when an MMA completes, and the
   // tile then landed a full loaded latency after the MMA was due (one stage per ~900 cycles).
-  static constexpr int XSTAGES_DEC = BM == 16 ? 16 : BM == 32 ? 12 : 5;
+  static constexpr int XSTAGES_DEC = BM == 16 ? BW_GEMM_XSTAGES16 : BM == 32 ? 12 : 5;
   static constexpr int STAGES_DEC = (208 * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES;
   static constexpr int STAGES = BM < 128 ? STAGES_DEC : STAGES_PRE;
   static constexpr int XSTAGES = BM < 128 ? XSTAGES_DEC : STAGES_PRE;
@@ -192,7 +201,9 @@ struct PCfg {
   static_assert(D_COL0 + DBUF * NI * BM <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(!ISSUER_X || XSTAGES >= 2 * NI, "activation ring too shallow for the issuers' look-ahead");
-  static_assert((2 * STAGES + 2 * XSTAGES + 2 * ASTAGES + 4 + 1) * 8 + 32 <= BAR_BYTES, "barrier area");
+  // barriers, then 32 bytes of slots (TMEM address, abort flag, ticket, epoch, trace record) and the
+  // deferred-reduction list (count + two entries of four ints)
+  static_assert((2 * STAGES + 2 * XSTAGES + 2 * ASTAGES + 4 + 1) * 8 + 32 + 48 <= BAR_BYTES, "barrier area");
   static_assert(X_PANEL % 1024 == 0 && OFF_X % 1024 == 0, "128-byte swizzled x tiles are 1024-byte aligned");
 };
 
@@ -323,6 +334,9 @@ __global__ void __launch_bounds__(512, 1)
   volatile int* ticket = abort_flag + 1;
   volatile uint32_t* sh_epoch = reinterpret_cast<volatile uint32_t*>(tmem_slot + 3);
   unsigned long long** trace_slot = reinterpret_cast<unsigned long long**>(tmem_slot + 4);
+  // stream-K tiles this CTA finishes last, reduced by all 512 threads after the main loop:
+  // pend[0] = count (<= 2: a CTA's first and last segments), entries {t, n_parts, c_first, poff0}
+  volatile int* pend = reinterpret_cast<volatile int*>(tmem_slot + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -347,6 +361,7 @@ __global__ void __launch_bounds__(512, 1)
     }
     mbar_init(final_bar, NI);
     *abort_flag = 0;
+    pend[0] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -383,6 +398,15 @@ __global__ void __launch_bounds__(512, 1)
         const int nt = sg.t / sc.m_tiles;
         for (int i = 0; i < sg.nkb; ++i, ++it) {
           const int s = it % STAGES;
+          if constexpr (BW_GEMM_W_GROUP > 1 && BM < 128) {
+            // wait for the group's last slot before issuing its first k-block (each slot's own wait follows)
+            const int jl = it + min(BW_GEMM_W_GROUP, sg.nkb - i) - 1;
+            if (i % BW_GEMM_W_GROUP == 0 && jl >= STAGES &&
+                !mbar_wait(&empty[jl % STAGES], ((jl / STAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
+              ok = false;
+              break;
+            }
+          }
           if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
             ok = false;
             break;
@@ -761,7 +785,17 @@ __global__ void __launch_bounds__(512, 1)
         named_bar_sync(1, 128);
         const bool last = *ticket == n_parts - 1;
         named_bar_sync(1, 128);  // every thread has read the ticket before the next segment overwrites it
-        if (last) {
+        if (!GLU && sc.mode == 1 && last) {
+          // the whole CTA sums this tile's pieces after the main loop
+          if (warp == 10 && lane == 0) {
+            const int i = pend[0];
+            pend[1 + 4 * i] = t;
+            pend[2 + 4 * i] = n_parts;
+            pend[3 + 4 * i] = c_first;
+            pend[4 + 4 * i] = static_cast<int>(poff0);
+            pend[0] = i + 1;
+          }
+        } else if (last) {
           __threadfence();
           const float scl = n < N ? load_as_float(srow, n, sdtype) : 0.f;
           // 8 columns at a time; the loads of four pieces are issued together, then summed
@@ -801,67 +835,154 @@ __global__ void __launch_bounds__(512, 1)
       }
     }
     if (warp == 10 && lane == 0) trace_stamp(trec, 3);
-    // (all four warps decide together: a barrier inside must see all of them)
-    if (g.world > 0 && !named_bar_any(1, 128, *abort_flag != 0)) {
-      // Receive: the (tile, peer) pairs are dealt to the CTAs round robin (the same on every rank;
-      // which peer CTA produced a tile does not matter).  A thread polls 8 words (16 outputs) at a
-      // time, the loads issued together; a word belongs to this call when its epoch does, and
-      // stale words (an older call of this parity) never do.  Bounded: a peer that never sends
-      // records the site and stops this CTA's receive.
-      const int peers = g.world - 1;
-      const int tiles = sc.m_tiles * sc.n_tiles;
-      const uint64_t* mbox = reinterpret_cast<const uint64_t*>(g.pad[g.rank] + kMailbox0);
-      const long long limit = wait_limit_cycles();
-      const long long tw0 = clock64();
-      bool ok = true;
-      for (int q = blockIdx.x; ok && q < tiles * peers; q += gridDim.x) {
-        const int t = q / peers;
-        const int p = q - t * peers + (q - t * peers >= g.rank ? 1 : 0);
-        const int nt = t / sc.m_tiles, mt = t - nt * sc.m_tiles;
-        const int rows = min(BM, M - mt * BM);
-        const uint64_t* src =
-            mbox + (static_cast<size_t>((epoch & 1u) * g.world + p) * M + mt * BM) * g.rowwords + nt * 64;
-        uint16_t* dst = reinterpret_cast<uint16_t*>(g.ybase) + static_cast<int64_t>(mt * BM) * ldy +
-                        static_cast<int64_t>(p) * g.n + nt * 128;
-        const int cols = min(128, g.n - nt * 128);
-        for (int w0 = row * 2; ok && w0 < rows * 64; w0 += 4 * 256) {
-          unsigned long long v[4][2];
+  }
+
+  // ---------------- all 512 threads, after the main loop ----------------
+  // (1) The stream-K tiles this CTA finished last: their pieces (up to ~20 at small per-rank N)
+  //     are summed with a float4 per thread and all loads of a batch in flight, in k order
+  //     (piece 0 first), so the result is the in-loop reduction's, bit for bit.
+  // (2) All-gather receive: the (tile, peer) pairs are dealt to the CTAs round robin (the same on
+  //     every rank; which peer CTA produced a tile does not matter).  A word belongs to this call
+  //     when its epoch does; stale words (an older call of this parity) never do.  Bounded: a peer
+  //     that never sends records the site and stops this CTA's receive.
+  // A CTA sends all it owns (its tiles and these reductions) before it receives anything.
+  if constexpr (!GLU) {
+    if (sc.mode == 1 || g.world > 0) {
+      __syncthreads();  // the pending list, the producers' drained rings
+      if (!__syncthreads_or(*abort_flag != 0)) {
+        const int tid = threadIdx.x;
+        const uint32_t ep = g.world > 0 ? *sh_epoch : 0u;
+        const int npend = pend[0];
+        uint16_t* stage = reinterpret_cast<uint16_t*>(sW);  // the weight ring is idle now
+        fence_proxy_async_smem();                          // its last writer was the TMA engine
+        constexpr size_t kPiece = static_cast<size_t>(128) * BM;
+        for (int i = 0; i < npend; ++i) {
+          const int t = pend[1 + 4 * i], n_parts = pend[2 + 4 * i], c_first = pend[3 + 4 * i];
+          const size_t poff0 = static_cast<size_t>(pend[4 + 4 * i]);
+          const int nt = t / sc.m_tiles;
+          const int m0 = (t - nt * sc.m_tiles) * BM;
+          const float* base = ws + static_cast<size_t>(c_first) * 2 * kPiece;
+          __threadfence();  // the contributors' pieces, published before their tickets
+          for (int f = tid; f < 32 * BM; f += C::THREADS) {
+            const int r = f / (BM / 4), c4 = (f % (BM / 4)) * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+            for (int p0 = 0; p0 < n_parts; p0 += 8) {
+              float4 v[8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int w = w0 + i * 256;
-            if (w < rows * 64) ld_ll2(src + static_cast<size_t>(w >> 6) * g.rowwords + (w & 63), v[i][0], v[i][1]);
-          }
+              for (int pp = 0; pp < 8; ++pp)
+                if (p0 + pp < n_parts)
+                  v[pp] = __ldcg(reinterpret_cast<const float4*>(base + (p0 + pp) * 2 * kPiece +
+                                                                 (p0 + pp == 0 ? poff0 : 0) + r * BM + c4));
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int w = w0 + i * 256;
-            if (w >= rows * 64) break;
-            const uint64_t* a = src + static_cast<size_t>(w >> 6) * g.rowwords + (w & 63);
-            while (static_cast<uint32_t>(v[i][0] >> 32) != epoch || static_cast<uint32_t>(v[i][1] >> 32) != epoch) {
-              if (clock64() - tw0 > limit) {
-                record_timeout(kSiteGRecv);
-                *abort_flag = 1;
-                ok = false;
-                break;
+              for (int pp = 0; pp < 8; ++pp) {
+                if (p0 + pp >= n_parts) break;
+                if (p0 + pp == 0) {
+                  acc = v[0];
+                } else {
+                  acc.x += v[pp].x;
+                  acc.y += v[pp].y;
+                  acc.z += v[pp].z;
+                  acc.w += v[pp].w;
+                }
               }
-              ld_ll2(a, v[i][0], v[i][1]);
             }
-            if (!ok) break;
-            // 4 outputs: token w / 64, columns 2 (w % 64) .. + 3 of the tile
-            const int c = 2 * (w & 63);
-            uint16_t* d = dst + static_cast<int64_t>(w >> 6) * ldy + c;
-            const uint32_t lo = static_cast<uint32_t>(v[i][0]), hi = static_cast<uint32_t>(v[i][1]);
-            if (g.vec4 && c + 4 <= cols) {
-              *reinterpret_cast<uint2*>(d) = make_uint2(lo, hi);
-            } else {
-              const uint16_t h4[4] = {static_cast<uint16_t>(lo), static_cast<uint16_t>(lo >> 16),
-                                      static_cast<uint16_t>(hi), static_cast<uint16_t>(hi >> 16)};
-              for (int u = 0; u < 4 && c + u < cols; ++u) d[u] = h4[u];
+            const int n = nt * 128 + r;
+            const float scl = n < N ? load_as_float(scale, n, sdtype) : 0.f;
+            const float o[4] = {acc.x * scl, acc.y * scl, acc.z * scl, acc.w * scl};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if constexpr (BF16) stage[(c4 + e) * 128 + r] = __bfloat16_as_ushort(__float2bfloat16_rn(o[e]));
+              else stage[(c4 + e) * 128 + r] = __half_as_ushort(__float2half_rn(o[e]));
             }
           }
+          __syncthreads();
+          const int n0 = nt * 128;
+          for (int cc = tid; cc < BM * 16; cc += C::THREADS) {
+            const int e = cc >> 4, c8 = (cc & 15) * 8;
+            const int m = m0 + e;
+            if (m >= M) continue;
+            const uint4 val = *reinterpret_cast<const uint4*>(stage + e * 128 + c8);
+            if (g.world > 0) {
+              const size_t off =
+                  (static_cast<size_t>((ep & 1u) * g.world + g.rank) * M + m) * g.rowwords + ((n0 + c8) >> 1);
+              for (int q = 0; q < g.world; ++q) {
+                if (q == g.rank) continue;
+                uint64_t* mb = reinterpret_cast<uint64_t*>(g.pad[q] + kMailbox0) + off;
+                st_ll2(mb, val.x, val.y, ep);
+                st_ll2(mb + 2, val.z, val.w, ep);
+              }
+            }
+            const int64_t idx = static_cast<int64_t>(m) * ldy + n0 + c8;
+            if (g.vec && n0 + c8 + 8 <= N) {
+              store_y8(y, idx, val);
+            } else {
+              const uint16_t* h = reinterpret_cast<const uint16_t*>(&val);
+              for (int q8 = 0; q8 < 8 && n0 + c8 + q8 < N; ++q8) static_cast<uint16_t*>(y)[idx + q8] = h[q8];
+            }
+          }
+          __syncthreads();  // the stage is read before the next tile overwrites it
+          if (tid == 0) counters[c_first] = 0;
+        }
+        if (tid == 0) trace_stamp(trec, 4);
+        if (g.world > 0) {
+          const int peers = g.world - 1;
+          const int tiles = sc.m_tiles * sc.n_tiles;
+          const uint64_t* mbox = reinterpret_cast<const uint64_t*>(g.pad[g.rank] + kMailbox0);
+          const long long limit = wait_limit_cycles();
+          const long long tw0 = clock64();
+          bool ok = true;
+          for (int q = blockIdx.x; ok && q < tiles * peers; q += gridDim.x) {
+            const int t = q / peers;
+            const int p = q - t * peers + (q - t * peers >= g.rank ? 1 : 0);
+            const int nt = t / sc.m_tiles, mt = t - nt * sc.m_tiles;
+            const int rows = min(BM, M - mt * BM);
+            const uint64_t* src =
+                mbox + (static_cast<size_t>((ep & 1u) * g.world + p) * M + mt * BM) * g.rowwords + nt * 64;
+            uint16_t* dst = reinterpret_cast<uint16_t*>(g.ybase) + static_cast<int64_t>(mt * BM) * ldy +
+                            static_cast<int64_t>(p) * g.n + nt * 128;
+            const int cols = min(128, g.n - nt * 128);
+            // 2 words (4 outputs) per thread per load, four loads in flight
+            for (int w0 = tid * 2; ok && w0 < rows * 64; w0 += 4 * 2 * C::THREADS) {
+              unsigned long long v[4][2];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int w = w0 + i * 2 * C::THREADS;
+                if (w < rows * 64) ld_ll2(src + static_cast<size_t>(w >> 6) * g.rowwords + (w & 63), v[i][0], v[i][1]);
+              }
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int w = w0 + i * 2 * C::THREADS;
+                if (w >= rows * 64) break;
+                const uint64_t* a = src + static_cast<size_t>(w >> 6) * g.rowwords + (w & 63);
+                while (static_cast<uint32_t>(v[i][0] >> 32) != ep || static_cast<uint32_t>(v[i][1] >> 32) != ep) {
+                  if (clock64() - tw0 > limit) {
+                    record_timeout(kSiteGRecv);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                  }
+                  ld_ll2(a, v[i][0], v[i][1]);
+                }
+                if (!ok) break;
+                // 4 outputs: token w / 64, columns 2 (w % 64) .. + 3 of the tile
+                const int c = 2 * (w & 63);
+                uint16_t* d = dst + static_cast<int64_t>(w >> 6) * ldy + c;
+                const uint32_t lo = static_cast<uint32_t>(v[i][0]), hi = static_cast<uint32_t>(v[i][1]);
+                if (g.vec4 && c + 4 <= cols) {
+                  *reinterpret_cast<uint2*>(d) = make_uint2(lo, hi);
+                } else {
+                  const uint16_t h4[4] = {static_cast<uint16_t>(lo), static_cast<uint16_t>(lo >> 16),
+                                          static_cast<uint16_t>(hi), static_cast<uint16_t>(hi >> 16)};
+                  for (int u = 0; u < 4 && c + u < cols; ++u) d[u] = h4[u];
+                }
+              }
+            }
+          }
+          __syncthreads();
+          if (tid == 0) trace_stamp(trec, 6);
         }
       }
-      named_bar_sync(1, 128);
-      if (warp == 10 && lane == 0) trace_stamp(trec, 6);
     }
   }
 
