@@ -150,7 +150,7 @@ __device__ __forceinline__ float round_out(float v) {
 // The weight producer requests this many consecutive k-blocks of the same rows back to back
 // (waiting for that many free slots), so a row's adjacent 128-byte blocks reach DRAM together.
 #ifndef BW_GEMM_W_GROUP
-#define BW_GEMM_W_GROUP 1
+#define BW_GEMM_W_GROUP 4
 #endif
 #ifndef BW_GEMM_DEC_ISSUERS
 #define BW_GEMM_DEC_ISSUERS 2
@@ -567,9 +567,23 @@ __global__ void __launch_bounds__(512, 1)
         if (it == 0 && threadIdx.x == 64) trace_stamp(trec, 1);
         const uint8_t* src = sW + s * C::W_BYTES + row * 128;
         uint32_t out[2][32];
+        // The row in registers, then the slot released before the conversion: the OR over every
+        // loaded word makes the arrive wait for the loads themselves (an arrive right after
+        // issuing them let a fast refill land under reads still in flight).  Releasing here
+        // instead of after the conversion measured +2.5 % on the 70B decode shapes (with
+        // BW_GEMM_W_GROUP = 4).
+        uint4 raw[8];
+        uint32_t dep = 0;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) raw[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
+#pragma unroll
+        for (int c = 0; c < 8; ++c) dep |= raw[c].x | raw[c].y | raw[c].z | raw[c].w;
+        asm volatile("" ::"r"(dep));  // `dep` (so every load) is complete before the arrive below
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const uint4 v = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
+          const uint4 v = raw[c];
           uint4 o0, o1;
           convert_chunk<BF16>(v, o0, o1);
           uint32_t* o = &out[c >> 2][8 * (c & 3)];
@@ -582,11 +596,6 @@ __global__ void __launch_bounds__(512, 1)
           o[6] = o1.z;
           o[7] = o1.w;
         }
-        // The weight slot is free once the whole warp has converted its rows: the converted
-        // values depend on every byte read, so the reads are complete before the release (an
-        // arrive right after the loads let a fast L2 refill land under reads still in flight).
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
         if (!mbar_wait(&aempty[t], pa ^ 1, abort_flag, kSitePConvA)) {
           ok = false;
           break;

@@ -85,14 +85,22 @@ __device__ __forceinline__ void lora_tile_epilogue(uint32_t taddr, uint8_t* sW, 
 // Persistent ΔW / merge: one CTA per SM walks a contiguous range of 128 x 128 output tiles in
 // row-major order, so a CTA keeps the row block's B[128, r] resident across its k-tiles and
 // streams only A[r, 128] panels (from L2: A is shared by every row block) and, for the merge,
-// the W tiles.  The MMA of tile i+1 runs while the epilogue of tile i converts and stores it
-// (double-buffered TMEM accumulators), and TMA stores overlap the next tile's epilogue.
+// the W tiles.  The MMA of tile i+1 runs while the epilogues of earlier tiles convert and store
+// them (one TMEM accumulator per epilogue group), and TMA stores overlap the next tile's epilogue.
 //   warp 0      TMA producer (B when the row block changes, A panels, W tiles)
 //   warp 1      TMEM owner and tcgen05.mma issuer (r/16 MMAs of M=N=128, K=16 per tile)
-//   warps 4-11  epilogue, two groups of four taking alternate tiles, thread = row: fp16(acc * s)
-//               (delta) or fp16(W + fp16(acc * s)) (merge), staged in the 128-byte-swizzled
-//               layout and written by TMA stores
+//   warps 4-15  epilogue, kLsGroups = 3 groups of four taking the tiles in turn, thread = row:
+//               fp16(acc * s) (delta) or fp16(W + fp16(acc * s)) (merge), staged in the
+//               128-byte-swizzled layout and written by TMA stores.  The epilogue bounds the
+//               launch (ΔW writes 32 KB per tile, read-modify-write for the merge): a third group
+//               measured faster than two on the 70B shapes.
 // ---------------------------------------------------------------------------
+constexpr int kLsGroups = 3;
+constexpr int kLsThreads = 128 + 128 * kLsGroups;
+constexpr int kLsSmemBudget = 220 * 1024;
+// barriers (A ring 2 x 6, B 2, W 2 x (kLsGroups + 1), accumulators 2 x kLsGroups, final) + 8 bytes
+static_assert((12 + 2 + 2 * (kLsGroups + 1) + 2 * kLsGroups + 1) * 8 + 8 <= 256, "barrier area");
+
 struct LoraStreamSmem {
   int rp, nbp, a_bytes, b_bytes, wslots, aslots, off_a, off_b, off_w, off_bar, total;
   __host__ __device__ LoraStreamSmem(int r, int mode) {
@@ -100,9 +108,11 @@ struct LoraStreamSmem {
     nbp = (rp + 63) / 64;
     a_bytes = ((2 * rp * 128 + 1023) / 1024) * 1024;
     b_bytes = nbp * 16384;
-    wslots = mode == kModeDelta ? 2 : 3;  // output staging, one per epilogue group (delta) / W tiles
-                                          // updated in place, one ahead of the two groups (merge)
-    const int left = 200 * 1024 - b_bytes - wslots * 32768;
+    // output staging (delta) / W tiles updated in place (merge), one per group; the merge takes a
+    // slot more (its producer one W tile ahead of the groups) where two A panels still fit
+    wslots = kLsGroups;
+    if (mode != kModeDelta && kLsSmemBudget - b_bytes - (kLsGroups + 1) * 32768 >= 2 * a_bytes) wslots = kLsGroups + 1;
+    const int left = kLsSmemBudget - b_bytes - wslots * 32768;
     aslots = left / a_bytes > 6 ? 6 : left / a_bytes;
     off_a = 0;
     off_b = off_a + aslots * a_bytes;
@@ -120,7 +130,7 @@ enum LoraStreamSite : int {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(kLsThreads, 1)
     lora_stream_kernel(const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
                        const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_out, int N,
                        int K, int r, float scaling) {
@@ -132,11 +142,11 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* aempty = afull + 6;                                      // [6]
   uint64_t* bfull = aempty + 6;
   uint64_t* bempty = bfull + 1;
-  uint64_t* wfull = bempty + 1;   // [3] merge: W tile landed
-  uint64_t* wempty = wfull + 3;   // [3] merge: the TMA store of the tile has read the slot
-  uint64_t* dfull = wempty + 3;   // [2]
-  uint64_t* dempty = dfull + 2;   // [2]
-  uint64_t* final_bar = dempty + 2;
+  uint64_t* wfull = bempty + 1;   // [kLsGroups + 1] merge: W tile landed
+  uint64_t* wempty = wfull + kLsGroups + 1;  // [kLsGroups + 1] merge: the tile's TMA store has read the slot
+  uint64_t* dfull = wempty + kLsGroups + 1;  // [kLsGroups]
+  uint64_t* dempty = dfull + kLsGroups;
+  uint64_t* final_bar = dempty + kLsGroups;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -153,11 +163,11 @@ __global__ void __launch_bounds__(384, 1)
     }
     mbar_init(bfull, 1);
     mbar_init(bempty, 1);
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < kLsGroups + 1; ++i) {
       mbar_init(&wfull[i], 1);
       mbar_init(&wempty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kLsGroups; ++i) {
       mbar_init(&dfull[i], 1);
       mbar_init(&dempty[i], 4);
     }
@@ -166,7 +176,7 @@ __global__ void __launch_bounds__(384, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);  // kLsGroups x 128 accumulator columns
     tmem_relinquish();
   }
   tc_fence_before();
@@ -231,8 +241,8 @@ __global__ void __launch_bounds__(384, 1)
       for (int i = 0; i < ntile; ++i) {
         const long long t = t_begin + i;
         const int rb = static_cast<int>(t / n_cb);
-        const int db = i & 1;
-        if (!mbar_wait(&dempty[db], ((i >> 1) & 1) ^ 1, abort_flag, kSiteLsMma)) break;
+        const int db = i % kLsGroups;
+        if (!mbar_wait(&dempty[db], ((i / kLsGroups) & 1) ^ 1, abort_flag, kSiteLsMma)) break;
         if (rb != prev_rb) {
           if (!mbar_wait(bfull, nb & 1, abort_flag, kSiteLsMma)) break;
           ++nb;
@@ -258,22 +268,22 @@ __global__ void __launch_bounds__(384, 1)
       mbar_wait(final_bar, 0, nullptr, kSiteLsDrain);
     }
   } else if (warp >= 4) {
-    // two epilogue groups (warps 4-7, 8-11) take alternate tiles, each with its own accumulator
-    // buffer (tile i: buffer i & 1) and named barrier; a group's leader issues its TMA stores and
-    // waits for them to read the staging slot before the group writes that slot again
+    // kLsGroups epilogue groups (warps 4-7, 8-11, 12-15) take the tiles in turn, each with its own
+    // accumulator (tile i: buffer i % kLsGroups) and named barrier; a group's leader issues its TMA
+    // stores and waits for them to read the staging slot before the group writes that slot again
     const int grp = (warp - 4) >> 2;
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const int bar_id = 1 + grp;
     const bool leader = (warp & 3) == 0 && lane == 0 && (warp >> 2) == 1 + grp;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    for (int i = grp; i < ntile; i += 2) {
+    for (int i = grp; i < ntile; i += kLsGroups) {
       const long long t = t_begin + i;
       const int rb = static_cast<int>(t / n_cb), cb = static_cast<int>(t % n_cb);
-      const int db = i & 1;
+      const int db = i % kLsGroups;
       const int sw = i % SW;
       uint8_t* sWt = smem + L.off_w + sw * 32768;
-      bool ok = mbar_wait(&dfull[db], (i >> 1) & 1, abort_flag, kSiteLsEpi);
+      bool ok = mbar_wait(&dfull[db], (i / kLsGroups) & 1, abort_flag, kSiteLsEpi);
       if constexpr (MODE != kModeDelta) ok = ok && mbar_wait(&wfull[sw], (i / SW) & 1, abort_flag, kSiteLsEpi);
       // one decision for the group; the leader's wait for its previous store is ordered before it
       if (named_bar_any(bar_id, 128, !ok || *abort_flag)) break;
@@ -299,7 +309,7 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -875,14 +885,14 @@ static int launch_lora_stream(const CUtensorMap& tb, const CUtensorMap& ta, cons
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&] {
-    // every rank's layout fits in the 200 KB planning budget plus barriers and alignment slack
+    // every rank's layout fits in the planning budget plus barriers and alignment slack
     err[dev & 63] = cudaFuncSetAttribute(lora_stream_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         200 * 1024 + 256 + 1024);
+                                         kLsSmemBudget + 256 + 1024);
   });
   if (int rc = check_cuda(err[dev & 63], "cudaFuncSetAttribute(lora_stream_kernel)")) return rc;
   const long long tiles = static_cast<long long>((N + 127) / 128) * ((K + 127) / 128);
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  lora_stream_kernel<MODE><<<grid, 384, L.total, st>>>(tb, ta, tw, to, N, K, r, s);
+  lora_stream_kernel<MODE><<<grid, kLsThreads, L.total, st>>>(tb, ta, tw, to, N, K, r, s);
   return check_launch("lora_stream_kernel");
 }
 
