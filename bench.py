@@ -1014,6 +1014,15 @@ def main():
             line["phases"] = phases
         print(json.dumps(line), flush=True)
     if world > 1:
+        # Teardown order: every CUDA graph (some hold NCCL work) was reset above; the workload's
+        # layers hold symmetric-memory signal pads, which are released here, on every rank, before
+        # the last collective and destroy_process_group (a symmetric-memory handle still alive at
+        # destroy is the remaining suspect of the one teardown that hung)
+        import gc
+
+        del wl
+        gc.collect()
+        torch.cuda.synchronize()
         # the result is out; bound the teardown so a stuck communicator cannot hold the GPUs
         import threading
 

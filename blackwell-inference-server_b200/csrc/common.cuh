@@ -23,6 +23,11 @@
 
 namespace bw {
 
+// GEMM workspaces start with a tile-counter region of this size for every split plan; the counters
+// are zero at rest, and anything else a caller keeps in a shared workspace must stay out of it.
+constexpr int kGemmCounterSlots = 1024;
+constexpr size_t kGemmCounterBytes = kGemmCounterSlots * sizeof(int);
+
 // ---------------------------------------------------------------------------
 // device status word (first failure wins) and the wait limit
 // ---------------------------------------------------------------------------

@@ -152,6 +152,11 @@ __device__ __forceinline__ float round_out(float v) {
 #ifndef BW_GEMM_W_GROUP
 #define BW_GEMM_W_GROUP 4
 #endif
+// Loads in flight per thread in the deferred stream-K reduction (a tile cut into up to ~20
+// pieces at small per-rank N).
+#ifndef BW_GEMM_RED_BATCH
+#define BW_GEMM_RED_BATCH 12
+#endif
 #ifndef BW_GEMM_DEC_ISSUERS
 #define BW_GEMM_DEC_ISSUERS 2
 #endif
@@ -211,8 +216,6 @@ struct PCfg {
 // so the fp32 pieces of one call never land where another shape keeps counters
 // (a workspace is shared by calls of different shapes): counters stay zero at
 // rest across any sequence of calls.
-constexpr int kGemmCounterSlots = 1024;
-constexpr size_t kGemmCounterBytes = kGemmCounterSlots * sizeof(int);
 
 // Work schedule of the persistent kernel.  A tile is 128 weight rows x BM tokens
 // (M-tile fastest: t = nt * m_tiles + mt) over `kblocks` k-blocks of 128.
@@ -865,6 +868,7 @@ __global__ void __launch_bounds__(512, 1)
         uint16_t* stage = reinterpret_cast<uint16_t*>(sW);  // the weight ring is idle now
         fence_proxy_async_smem();                          // its last writer was the TMA engine
         constexpr size_t kPiece = static_cast<size_t>(128) * BM;
+        constexpr int kRedBatch = BW_GEMM_RED_BATCH;  // pieces loaded together per thread
         for (int i = 0; i < npend; ++i) {
           const int t = pend[1 + 4 * i], n_parts = pend[2 + 4 * i], c_first = pend[3 + 4 * i];
           const size_t poff0 = static_cast<size_t>(pend[4 + 4 * i]);
@@ -876,15 +880,15 @@ __global__ void __launch_bounds__(512, 1)
             const int r = f / (BM / 4), c4 = (f % (BM / 4)) * 4;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-            for (int p0 = 0; p0 < n_parts; p0 += 8) {
-              float4 v[8];
+            for (int p0 = 0; p0 < n_parts; p0 += kRedBatch) {
+              float4 v[kRedBatch];
 #pragma unroll
-              for (int pp = 0; pp < 8; ++pp)
+              for (int pp = 0; pp < kRedBatch; ++pp)
                 if (p0 + pp < n_parts)
                   v[pp] = __ldcg(reinterpret_cast<const float4*>(base + (p0 + pp) * 2 * kPiece +
                                                                  (p0 + pp == 0 ? poff0 : 0) + r * BM + c4));
 #pragma unroll
-              for (int pp = 0; pp < 8; ++pp) {
+              for (int pp = 0; pp < kRedBatch; ++pp) {
                 if (p0 + pp >= n_parts) break;
                 if (p0 + pp == 0) {
                   acc = v[0];
@@ -1076,6 +1080,19 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false, boo
 #define BW_GEMM_PART_COST_SCALE 1.0
 #endif
   const double part_cost = BW_GEMM_PART_COST_SCALE * 2.0 * 128 * p.bm * 4;
+  // Small decode GEMMs (at most 8 k-blocks per CTA even on `cap` CTAs, e.g. every Qwen3-0.6B
+  // projection) use at most `cap` CTAs: they are bound by per-launch latency, and the SMs left
+  // over host the next launch's CTAs, which stream their weights while this launch finishes
+  // (programmatic dependent launch).  32 measured cfg1 415 -> 567 GB/s, cfg3 337 -> 425 GB/s
+  // against all 148 SMs.
+#ifndef BW_GEMM_SPLITK_CAP
+#define BW_GEMM_SPLITK_CAP 32
+#endif
+  const int64_t work_kb = tiles * p.kblocks;
+  const int cap = p.bm < 128 && BW_GEMM_SPLITK_CAP > 0 && BW_GEMM_SPLITK_CAP < sms &&
+                          work_kb <= 8LL * BW_GEMM_SPLITK_CAP
+                      ? BW_GEMM_SPLITK_CAP
+                      : sms;
   double best = 1e300;
   int64_t best_per_cta = 1;
   for (int sp = 1; sp <= p.kblocks && sp <= 32; ++sp) {
@@ -1083,7 +1100,7 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false, boo
     const int real = (p.kblocks + kbps - 1) / kbps;
     if (real != sp) continue;
     const int64_t units = tiles * sp;
-    const int64_t per_cta = (units + sms - 1) / sms;
+    const int64_t per_cta = (units + cap - 1) / cap;
     const double unit_cost = kbps * 16384.0 + 6000.0 + (sp > 1 ? part_cost : 0.0);
     const double cost = static_cast<double>(per_cta) * unit_cost;
     if (cost < best * 0.97) {
@@ -1124,7 +1141,7 @@ static GemmPlan plan_gemm(int64_t m, int64_t n, int64_t k, bool glu = false, boo
   }
   const int64_t units = tiles * p.splits;
   p.units = units > INT32_MAX ? -1 : static_cast<int>(units);  // -1: too many units (refused by the caller)
-  p.grid = units < sms ? static_cast<int>(units) : sms;
+  p.grid = units < cap ? static_cast<int>(units) : cap;
   if (p.splits > 1) {
     if (tiles > kGemmCounterSlots) {  // unreachable for realistic shapes: work < sms with > 1024 tiles
       p.splits = 1;

@@ -95,9 +95,12 @@ static int check_norm_args(const void* x, int dtype, int64_t ldx, const void* w,
   return BW_OK;
 }
 
-// normalised rows go to the workspace after the GEMM's own scratch, 256-byte aligned
+// Normalised rows go to the workspace after the GEMM's own scratch, 256-byte aligned, and never
+// into the GEMM counter region: a plan without split tiles needs no scratch, but a workspace is
+// shared with other calls, whose tile counters at its start must stay zero.
 static size_t norm_offset(int64_t m, int64_t n, int64_t k) {
-  return (bw_w8a16_gemm_workspace_size(m, n, k) + 255) / 256 * 256;
+  const size_t g = bw_w8a16_gemm_workspace_size(m, n, k);
+  return ((g > kGemmCounterBytes ? g : kGemmCounterBytes) + 255) / 256 * 256;
 }
 
 }  // namespace bw

@@ -95,3 +95,23 @@ def test_int8_gemm_rmsnorm(cuda_dev, dt, m, n, k, with_res):
     from blackwell_ops import _lib
 
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 3072, 1024), (16, 3072, 1024), (16, 1024, 4096)])
+def test_prologue_leaves_shared_counters_zero(cuda_dev, m, n, k):
+    """The normalised rows live in the caller's workspace, which int8_gemm shares: whatever the
+    GEMM's plan (with or without split tiles), the counter region at its start stays zero."""
+    from blackwell_ops import _lib
+    from blackwell_ops.kernels import int8_gemm_rmsnorm
+    from blackwell_ops.kernels.int8_gemm import _workspaces
+
+    g = torch.Generator(device=cuda_dev).manual_seed(m + n + k)
+    x = torch.randn(m, k, generator=g, device=cuda_dev).half()
+    nw = torch.randn(k, generator=g, device=cuda_dev).half()
+    q = torch.randint(-127, 128, (n, k), generator=g, device=cuda_dev, dtype=torch.int8)
+    s = (torch.rand(n, generator=g, device=cuda_dev) * 1e-3 + 1e-4).half()
+    int8_gemm_rmsnorm(x, None, nw, q, s)
+    torch.cuda.synchronize()
+    ws = _workspaces[(cuda_dev.index if cuda_dev.index is not None else torch.cuda.current_device(),
+                      _lib.stream_ptr(cuda_dev))]
+    assert int(ws[:4096].count_nonzero()) == 0
