@@ -53,12 +53,14 @@ def test_gemm_workspace_contract_host_only():
     from blackwell_ops import _lib
 
     lib = _lib.lib
-    shapes = [(16, 3072, 1024), (16, 1024, 3072), (16, 151936, 1024), (16, 28672, 8192), (64, 3072, 8192)]
+    shapes = [(16, 1024, 4096), (16, 1024, 3072), (16, 151936, 1024), (16, 28672, 8192), (64, 3072, 8192)]
     for m, n, k in shapes:
         need = lib.bw_w8a16_gemm_workspace_size(m, n, k)
         zeroed = lib.bw_w8a16_gemm_workspace_zeroed_bytes(m, n, k)
         assert need > 0 and zeroed == 4096 and need % 16 == 0, (m, n, k, need, zeroed)
-    # one CTA per tile with the whole K: no pieces, no counters
+    # one CTA per tile with the whole K: no pieces, no counters (prefill; and a small decode GEMM,
+    # which runs on at most 32 CTAs)
+    assert lib.bw_w8a16_gemm_workspace_size(16, 3072, 1024) == 0
     assert lib.bw_w8a16_gemm_workspace_size(2048, 14336, 4096) == 0
     assert lib.bw_w8a16_gemm_workspace_zeroed_bytes(2048, 14336, 4096) == 0
     # LM head at M=16: stream-K over 148 CTAs, two 128 x 16 fp32 pieces per CTA after the counters
