@@ -59,6 +59,10 @@ SIGNATURES = {
     "bw_w8a16_gemm_allgather": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
                                            _I64, _c.POINTER(_c.c_void_p), _c.c_size_t, _c.c_int, _c.c_int, _P,
                                            _c.c_size_t, _P]),
+    "bw_debug_streamk_walk": (_c.c_int, [_I64, _I64, _c.c_int, _c.c_int, _P, _c.c_int]),
+    "bw_debug_streamk_start": (_I64, [_I64, _I64, _c.c_int, _c.c_int]),
+    "bw_debug_streamk_owner": (_c.c_int, [_I64, _I64, _c.c_int, _I64]),
+    "bw_debug_streamk_pieces": (_c.c_int, [_I64, _I64, _c.c_int, _c.c_int, _P]),
     "bw_lora_delta": (_c.c_int, [_P, _P, _P, _I64, _I64, _I64, _c.c_float, _P]),
     "bw_add_delta": (_c.c_int, [_P, _P, _I64, _P]),
     "bw_lora_merge": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),

@@ -244,11 +244,11 @@ struct Seg {
 
 // Stream-K plans keep work * grid below 2^31 (checked by the planner), so the
 // range arithmetic is 32-bit.
-__device__ __forceinline__ long long sk_start(long long b, const Sched& s, int grid) {
+__host__ __device__ __forceinline__ long long sk_start(long long b, const Sched& s, int grid) {
   return static_cast<long long>(static_cast<unsigned>(b) * static_cast<unsigned>(s.work) / static_cast<unsigned>(grid));
 }
 // the CTA whose stream-K range holds k-block x of the flattened work
-__device__ __forceinline__ int sk_owner(long long x, const Sched& s, int grid) {
+__host__ __device__ __forceinline__ int sk_owner(long long x, const Sched& s, int grid) {
   const unsigned w = static_cast<unsigned>(s.work);
   return static_cast<int>((static_cast<unsigned>(x + 1) * static_cast<unsigned>(grid) + w - 1) / w) - 1;
 }
@@ -257,13 +257,13 @@ struct SegWalk {
   long long x, end;
   int u, grid;
   bool first;
-  __device__ __forceinline__ SegWalk(const Sched& s, int b, int g) : x(0), end(0), u(b), grid(g), first(true) {
+  __host__ __device__ __forceinline__ SegWalk(const Sched& s, int b, int g) : x(0), end(0), u(b), grid(g), first(true) {
     if (s.mode == 1) {
       x = sk_start(b, s, g);
       end = sk_start(b + 1, s, g);
     }
   }
-  __device__ __forceinline__ bool next(const Sched& s, Seg& sg) {
+  __host__ __device__ __forceinline__ bool next(const Sched& s, Seg& sg) {
     if (s.mode == 0) {
       if (u >= s.units) return false;
       sg.split = u % s.splits;
@@ -285,6 +285,22 @@ struct SegWalk {
     return true;
   }
 };
+
+// Where the pieces of a cut stream-K tile t live: the first contributor `c_first` (whose counter
+// the contributors count on), the number of contributors, and the slot (0: the CTA's first
+// segment, 1: a later one) of the first contributor's piece; every later contributor starts its
+// range inside the tile, so its piece is in its slot 0.
+struct PieceLoc {
+  int c_first, n_parts, slot0;
+};
+__host__ __device__ __forceinline__ PieceLoc sk_pieces(const Sched& s, int t, int grid) {
+  const long long kb = s.kblocks;
+  PieceLoc p;
+  p.c_first = sk_owner(t * kb, s, grid);
+  p.n_parts = sk_owner(t * kb + kb - 1, s, grid) - p.c_first + 1;
+  p.slot0 = sk_start(p.c_first, s, grid) / kb == t ? 0 : 1;
+  return p;
+}
 
 enum PersistentWaitSite : int {
   kSitePProd = 111,
@@ -756,9 +772,9 @@ __global__ void __launch_bounds__(512, 1)
         if (lane == 0) mbar_arrive(&dempty[b]);
       } else {
         // piece slots: [tile][split] (mode 0) or [cta][first/last segment] (mode 1)
-        const long long kb = sc.kblocks;
-        const int c_first = sc.mode == 0 ? 0 : sk_owner(t * kb, sc, gridDim.x);
-        const int n_parts = sc.mode == 0 ? sc.splits : sk_owner(t * kb + kb - 1, sc, gridDim.x) - c_first + 1;
+        const PieceLoc loc = sc.mode == 0 ? PieceLoc{0, sc.splits, 0} : sk_pieces(sc, t, gridDim.x);
+        const int c_first = loc.c_first;
+        const int n_parts = loc.n_parts;
         // piece c of the tile sits at base + c * stride (+ off0 for piece 0): in mode 1 every
         // contributor after the first starts its range inside the tile (its slot 0), and only
         // the first may hold the tile as its last segment (slot 1).  Branch-free addresses keep
@@ -772,7 +788,7 @@ __global__ void __launch_bounds__(512, 1)
         } else {
           pbase = ws + static_cast<size_t>(c_first) * 2 * kPiece + static_cast<size_t>(row) * BM;
           pstride = 2 * kPiece;
-          poff0 = sk_start(c_first, sc, gridDim.x) / kb == t ? 0 : kPiece;
+          poff0 = loc.slot0 ? kPiece : 0;
         }
         // tile counter: the tile itself (mode 0) or the CTA holding its first k-block, which
         // heads at most one cut tile (mode 1); either way an index below kGemmCounterSlots
@@ -1459,4 +1475,60 @@ extern "C" int bw_w8a16_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, co
     }
   }
   return bw_w8a16_gemm(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y, ldy, m, n, k, nullptr, 0, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Stream-K schedule introspection (host only, for tests): the same sk_start / sk_owner / SegWalk /
+// sk_pieces code the kernel runs, on a plan of `tiles` tiles of `kblocks` k-blocks over `grid` CTAs.
+// ---------------------------------------------------------------------------
+static bool streamk_plan(int64_t kblocks, int64_t tiles, int grid, bw::Sched* s) {
+  if (kblocks < 1 || tiles < 1 || grid < 1 || kblocks * tiles < grid || kblocks * tiles * grid >= (1LL << 31))
+    return false;
+  *s = bw::Sched{};
+  s->mode = 1;
+  s->n_tiles = static_cast<int>(tiles);
+  s->m_tiles = 1;
+  s->kblocks = static_cast<int>(kblocks);
+  s->work = kblocks * tiles;
+  return true;
+}
+
+extern "C" int bw_debug_streamk_walk(int64_t kblocks, int64_t tiles, int grid, int cta, int32_t* segs,
+                                     int max_segs) {
+  bw::Sched s;
+  if (!streamk_plan(kblocks, tiles, grid, &s) || cta < 0 || cta >= grid || !segs) return -1;
+  bw::SegWalk wk(s, cta, grid);
+  bw::Seg sg;
+  int n = 0;
+  while (wk.next(s, sg)) {
+    if (n >= max_segs) return -1;
+    segs[4 * n] = sg.t;
+    segs[4 * n + 1] = sg.k0;
+    segs[4 * n + 2] = sg.nkb;
+    segs[4 * n + 3] = sg.split;
+    ++n;
+  }
+  return n;
+}
+
+extern "C" int64_t bw_debug_streamk_start(int64_t kblocks, int64_t tiles, int grid, int cta) {
+  bw::Sched s;
+  if (!streamk_plan(kblocks, tiles, grid, &s) || cta < 0 || cta > grid) return -1;
+  return bw::sk_start(cta, s, grid);
+}
+
+extern "C" int bw_debug_streamk_owner(int64_t kblocks, int64_t tiles, int grid, int64_t x) {
+  bw::Sched s;
+  if (!streamk_plan(kblocks, tiles, grid, &s) || x < 0 || x >= s.work) return -1;
+  return bw::sk_owner(x, s, grid);
+}
+
+extern "C" int bw_debug_streamk_pieces(int64_t kblocks, int64_t tiles, int grid, int tile, int32_t* loc) {
+  bw::Sched s;
+  if (!streamk_plan(kblocks, tiles, grid, &s) || tile < 0 || tile >= tiles || !loc) return -1;
+  const bw::PieceLoc p = bw::sk_pieces(s, tile, grid);
+  loc[0] = p.c_first;
+  loc[1] = p.n_parts;
+  loc[2] = p.slot0;
+  return 0;
 }

@@ -145,6 +145,22 @@ int bw_w8a16_gemm_allgather(const void* x, int x_dtype, int64_t ldx, const int8_
                             size_t workspace_bytes, void* stream);
 
 /*
+ * Stream-K schedule introspection (host only, no device work; used by the tests to check the
+ * schedule code the GEMM kernel itself runs).  A plan of `tiles` tiles of `kblocks` k-blocks over
+ * `grid` CTAs (kblocks * tiles >= grid, kblocks * tiles * grid < 2^31):
+ *   _walk:   CTA `cta`'s segments as {tile, first k-block, k-blocks, slot} quadruples into segs
+ *            (at most max_segs); returns their count, -1 on invalid arguments.
+ *   _start:  first flattened k-block of CTA `cta` (cta == grid: the end of the work).
+ *   _owner:  the CTA whose range holds flattened k-block x.
+ *   _pieces: tile `tile`'s first contributor, number of contributors and the first contributor's
+ *            piece slot, into loc[0..2].
+ */
+int bw_debug_streamk_walk(int64_t kblocks, int64_t tiles, int grid, int cta, int32_t* segs, int max_segs);
+int64_t bw_debug_streamk_start(int64_t kblocks, int64_t tiles, int grid, int cta);
+int bw_debug_streamk_owner(int64_t kblocks, int64_t tiles, int grid, int64_t x);
+int bw_debug_streamk_pieces(int64_t kblocks, int64_t tiles, int grid, int tile, int32_t* loc);
+
+/*
  * LoRA delta: delta[n, k] = fp16( fp32(sum_j b[n,j] * a[j,k]) * scaling ).
  * Replaces lora_delta (src/blackwell_ops/cuda/lora_ops.cu:43-60) and
  * lora_delta_tiled (src/blackwell_ops/cuda/lora_tiled.cu:88-103).
