@@ -129,9 +129,12 @@ class MultiDeltaLoRAModel:
     """
 
     def __init__(self, base: str | torch.nn.Module, device: str = "cuda", tokenizer=None,
-                 targets: Iterable[str] = DEFAULT_TARGETS, quantize: bool = True):
+                 targets: Iterable[str] = DEFAULT_TARGETS, quantize: bool = True, exact: bool = False):
         self.device = device
         self.quantize = quantize
+        # exact=True: adapters merged with the reference's own accumulation order (CUDA cores), so
+        # every int8 copy equals quantize_weight_int8(add_delta_(W, lora_delta(A, B, s))) bit for bit
+        self.exact = exact
         self.targets = tuple(targets)
         if isinstance(base, (str, Path)):
             from transformers import AutoModelForCausalLM, AutoTokenizer
@@ -199,7 +202,8 @@ class MultiDeltaLoRAModel:
                 if layer.base_weight is None:
                     raise RuntimeError("a layer was built without its fp16 base weight; cannot merge adapters")
             outs = lora_merge_requant_batched(
-                (layer.base_weight, used[n][0], used[n][1], used[n][2]) for n, layer in zip(names, layers))
+                ((layer.base_weight, used[n][0], used[n][1], used[n][2]) for n, layer in zip(names, layers)),
+                exact=self.exact)
             # adapter loading is not on the serving path: synchronise and raise if a device wait of
             # the batched requantisation ran out (its codes would be incomplete)
             from blackwell_ops.device import check
@@ -238,7 +242,7 @@ class MultiDeltaLoRAModel:
                 base = self._fp16_base[layer_name]
                 if layer_name in entries:
                     A, B, s = entries[layer_name]
-                    lora_merge(base, A, B, s, out=module.weight.data)
+                    lora_merge(base, A, B, s, out=module.weight.data, exact=self.exact)
                 else:
                     module.weight.data.copy_(base)
         self._current_adapter = adapter_name

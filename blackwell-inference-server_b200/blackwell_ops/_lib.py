@@ -65,6 +65,8 @@ SIGNATURES = {
     "bw_debug_streamk_pieces": (_c.c_int, [_I64, _I64, _c.c_int, _c.c_int, _P]),
     "bw_lora_delta": (_c.c_int, [_P, _P, _P, _I64, _I64, _I64, _c.c_float, _P]),
     "bw_add_delta": (_c.c_int, [_P, _P, _I64, _P]),
+    "bw_lora_delta_exact": (_c.c_int, [_P, _P, _P, _I64, _I64, _I64, _c.c_float, _P]),
+    "bw_lora_merge_exact": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),
     "bw_lora_merge": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _I64, _I64, _I64, _P]),
     "bw_lora_merge_requant_workspace_size": (_c.c_size_t, [_I64, _I64, _I64]),
     "bw_lora_merge_requant": (_c.c_int, [_P, _I64, _P, _P, _c.c_float, _P, _I64, _P, _I64, _I64, _I64, _P,

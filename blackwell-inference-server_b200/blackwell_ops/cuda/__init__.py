@@ -68,8 +68,12 @@ def _check_ab(A: torch.Tensor, B: torch.Tensor) -> tuple[int, int, int]:
     return r, K, N
 
 
-def lora_delta(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0) -> torch.Tensor:
-    """A: [r, K], B: [N, r] -> delta: [N, K] = B @ A * scaling (fp16, fp32 accumulation)"""
+def lora_delta(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0, exact: bool = False) -> torch.Tensor:
+    """A: [r, K], B: [N, r] -> delta: [N, K] = B @ A * scaling (fp16, fp32 accumulation).
+
+    ``exact=True`` sums on the CUDA cores in the reference kernels' j order, so the result equals
+    the reference bit for bit (the tensor-core default is within one fp16 ulp, < 1 % of values
+    differing)."""
     r, K, N = _check_ab(A, B)
     A = A.contiguous()
     B = B.contiguous()
@@ -78,14 +82,15 @@ def lora_delta(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0) -> torch.
         if r == 0:
             return delta.zero_()
         with torch.cuda.device(A.device):
-            check(lib.bw_lora_delta(A.data_ptr(), B.data_ptr(), delta.data_ptr(), N, K, r, float(scaling),
-                                    stream_ptr(A.device)), "lora_delta")
+            fn = lib.bw_lora_delta_exact if exact else lib.bw_lora_delta
+            check(fn(A.data_ptr(), B.data_ptr(), delta.data_ptr(), N, K, r, float(scaling), stream_ptr(A.device)),
+                  "lora_delta")
     return delta
 
 
-def lora_delta_tiled(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0) -> torch.Tensor:
+def lora_delta_tiled(A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0, exact: bool = False) -> torch.Tensor:
     """A: [r, K], B: [N, r] -> delta: [N, K] = B @ A * scaling (same kernel as lora_delta)"""
-    return lora_delta(A, B, scaling)
+    return lora_delta(A, B, scaling, exact=exact)
 
 
 def add_delta_(W: torch.Tensor, delta: torch.Tensor) -> None:
@@ -124,8 +129,9 @@ def _check_w(W: torch.Tensor, N: int, K: int) -> torch.Tensor:
 
 
 def lora_merge(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0,
-               out: torch.Tensor | None = None) -> torch.Tensor:
-    """W' = fp16(W + fp16(B @ A * scaling)); ``out=W`` merges in place."""
+               out: torch.Tensor | None = None, exact: bool = False) -> torch.Tensor:
+    """W' = fp16(W + fp16(B @ A * scaling)); ``out=W`` merges in place.  ``exact=True``: the
+    reference's j-ordered accumulation on the CUDA cores (bit-exact with add_delta_(W, lora_delta))."""
     r, K, N = _check_ab(A, B)
     W = _check_w(W, N, K)
     A = A.contiguous()
@@ -140,18 +146,27 @@ def lora_merge(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor, scaling: float
                 out.copy_(W)
             return out
         with torch.cuda.device(W.device):
-            check(lib.bw_lora_merge(W.data_ptr(), W.stride(0), A.data_ptr(), B.data_ptr(), float(scaling),
-                                    out.data_ptr(), out.stride(0), N, K, r, stream_ptr(W.device)), "lora_merge")
+            fn = lib.bw_lora_merge_exact if exact else lib.bw_lora_merge
+            check(fn(W.data_ptr(), W.stride(0), A.data_ptr(), B.data_ptr(), float(scaling), out.data_ptr(),
+                     out.stride(0), N, K, r, stream_ptr(W.device)), "lora_merge")
     return out
 
 
-def lora_merge_requant(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
-                       scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
-    """(w_int8, scale) = quantize_weight_int8(lora_merge(W, A, B, scaling)), fused."""
+def lora_merge_requant(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor, scaling: float = 1.0,
+                       exact: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """(w_int8, scale) = quantize_weight_int8(lora_merge(W, A, B, scaling)), fused.
+
+    ``exact=True`` merges with the reference's j-ordered accumulation on the CUDA cores into a
+    temporary fp16 weight and quantises that, so codes and scales equal the reference pipeline
+    (``quantize_weight_int8(add_delta_(W, lora_delta(A, B, s)))``) bit for bit."""
     r, K, N = _check_ab(A, B)
     W = _check_w(W, N, K)
     if K == 0:
         raise RuntimeError("lora_merge_requant: Expected reduction dim -1 to have non-zero size")
+    if exact:
+        from ..kernels import quantize_weight_int8
+
+        return quantize_weight_int8(lora_merge(W, A, B, scaling, exact=True))
     A = A.contiguous()
     B = B.contiguous()
     q = torch.empty((N, K), dtype=torch.int8, device=W.device)
@@ -173,15 +188,17 @@ def lora_merge_requant(W: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
     return q, scale
 
 
-def lora_merge_requant_batched(items):
+def lora_merge_requant_batched(items, exact: bool = False):
     """Fused merge + requantisation of several projections in as few launches as possible.
 
     ``items``: iterable of ``(W, A, B, scaling)`` on one device.  Returns a list
-    of ``(w_int8, scale)``, each equal to ``lora_merge_requant(W, A, B, scaling)``.
+    of ``(w_int8, scale)``, each equal to ``lora_merge_requant(W, A, B, scaling, exact)``.
     """
     items = list(items)
     if not items:
         return []
+    if exact:
+        return [lora_merge_requant(W, A, B, s, exact=True) for W, A, B, s in items]
     keep, outs, probs = [], [], []
     dev = None
     for W, A, B, scaling in items:

@@ -824,6 +824,70 @@ __global__ void lora_simt_kernel(const __half* __restrict__ A, const __half* __r
   out[static_cast<int64_t>(n) * ldo + k] = d;
 }
 
+// Reference-order delta / merge on the CUDA cores (the `exact` entry points): every output is the
+// reference kernels' own j-ordered fp32 accumulation, acc = fmaf(B[n,j], A[j,k], acc) for
+// j = 0 .. r-1, rounded as they round it (lora_ops.cu:16-27, :32-38), so delta, the merged weight
+// and its requantisation equal the reference pipeline bit for bit.  A thread computes 4 rows x 4
+// columns; the block's 16 rows of B sit in shared memory as fp32, A is read 4 columns at a time.
+constexpr int kExactRows = 16;
+constexpr int kExactMaxR = 1024;  // 64 KB of B rows in shared memory
+
+template <int MODE, bool VEC>
+__global__ void __launch_bounds__(128) lora_exact_kernel(const __half* __restrict__ A, const __half* __restrict__ B,
+                                                         const __half* W, int64_t ldw, __half* out, int64_t ldo, int N,
+                                                         int K, int r, float s) {
+  extern __shared__ float sB[];  // [kExactRows][r]
+  const int n0 = blockIdx.y * kExactRows;
+  for (int i = threadIdx.x; i < kExactRows * r; i += blockDim.x) {
+    const int rr = i / r;
+    sB[i] = n0 + rr < N ? __half2float(B[static_cast<int64_t>(n0 + rr) * r + (i - rr * r)]) : 0.f;
+  }
+  __syncthreads();
+  const int cg = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int k0 = blockIdx.x * 128 + cg * 4;
+  if (k0 >= K) return;
+  float acc[4][4];
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[rr][e] = 0.f;
+  const float* brow = sB + rg * 4 * r;
+  for (int j = 0; j < r; ++j) {
+    float a[4];
+    const __half* ap = A + static_cast<int64_t>(j) * K + k0;
+    if constexpr (VEC) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(ap));
+      a[0] = h2f_lo(v.x);
+      a[1] = h2f_hi(v.x);
+      a[2] = h2f_lo(v.y);
+      a[3] = h2f_hi(v.y);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) a[e] = k0 + e < K ? __half2float(ap[e]) : 0.f;
+    }
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const float b = brow[rr * r + j];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[rr][e] = fmaf(b, a[e], acc[rr][e]);
+    }
+  }
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr) {
+    const int n = n0 + rg * 4 + rr;
+    if (n >= N) break;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int k = k0 + e;
+      if (k >= K) break;
+      __half d = __float2half_rn(acc[rr][e] * s);
+      if constexpr (MODE == kModeMerge)
+        d = __float2half_rn(__half2float(W[static_cast<int64_t>(n) * ldw + k]) + __half2float(d));
+      out[static_cast<int64_t>(n) * ldo + k] = d;
+    }
+  }
+}
+
 // Fused merge + requantise for layouts TMA cannot address: one block per row,
 // two passes that both recompute the merged row (the reference's j-ordered
 // fp32 accumulation), so no scratch memory is needed.
@@ -1099,6 +1163,65 @@ extern "C" int bw_lora_merge(const void* w, int64_t ldw, const void* a, const vo
   if (int s = make_tmap_2d(&to, w_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n, k, ldo * 2, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
     return s;
   return launch_lora_stream<kModeMerge>(tb, ta, tw, to, (int)n, (int)k, (int)r, scaling, st);
+}
+
+namespace bw {
+static int launch_lora_exact(int mode, const void* a, const void* b, const void* w, int64_t ldw, void* out,
+                             int64_t ldo, int64_t n, int64_t k, int64_t r, float s, cudaStream_t st) {
+  if (r > kExactMaxR) {  // B rows beyond shared memory: the one-output-per-thread kernel (same order)
+    dim3 grid(static_cast<unsigned>((k + 127) / 128), static_cast<unsigned>(n));
+    lora_simt_kernel<<<grid, 128, 0, st>>>(static_cast<const __half*>(a), static_cast<const __half*>(b),
+                                           static_cast<const __half*>(w), ldw, static_cast<__half*>(out), ldo, (int)n,
+                                           (int)k, (int)r, s, mode);
+    return check_launch("lora_simt_kernel");
+  }
+  const dim3 grid(static_cast<unsigned>((k + 127) / 128), static_cast<unsigned>((n + kExactRows - 1) / kExactRows));
+  const size_t smem = static_cast<size_t>(kExactRows) * r * sizeof(float);
+  const bool vec = k % 4 == 0 && reinterpret_cast<uintptr_t>(a) % 8 == 0;
+  const __half* A = static_cast<const __half*>(a);
+  const __half* B = static_cast<const __half*>(b);
+  const __half* W = static_cast<const __half*>(w);
+  __half* O = static_cast<__half*>(out);
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [] {
+    const int bytes = kExactRows * kExactMaxR * sizeof(float);
+    cudaFuncSetAttribute(lora_exact_kernel<kModeDelta, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(lora_exact_kernel<kModeDelta, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(lora_exact_kernel<kModeMerge, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(lora_exact_kernel<kModeMerge, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  if (mode == kModeDelta) {
+    if (vec) lora_exact_kernel<kModeDelta, true><<<grid, 128, smem, st>>>(A, B, W, ldw, O, ldo, (int)n, (int)k, (int)r, s);
+    else lora_exact_kernel<kModeDelta, false><<<grid, 128, smem, st>>>(A, B, W, ldw, O, ldo, (int)n, (int)k, (int)r, s);
+  } else {
+    if (vec) lora_exact_kernel<kModeMerge, true><<<grid, 128, smem, st>>>(A, B, W, ldw, O, ldo, (int)n, (int)k, (int)r, s);
+    else lora_exact_kernel<kModeMerge, false><<<grid, 128, smem, st>>>(A, B, W, ldw, O, ldo, (int)n, (int)k, (int)r, s);
+  }
+  return check_launch("lora_exact_kernel");
+}
+}  // namespace bw
+
+extern "C" int bw_lora_delta_exact(const void* a, const void* b, void* delta, int64_t n, int64_t k, int64_t r,
+                                   float scaling, void* stream) {
+  using namespace bw;
+  if (int s = check_lora_args("lora_delta", a, b, n, k, r)) return s;
+  if (n == 0 || k == 0) return BW_OK;
+  if (!delta) return fail(BW_ERR_INVALID_ARGUMENT, "lora_delta: null output");
+  if (int s = require_sm100()) return s;
+  return launch_lora_exact(kModeDelta, a, b, nullptr, 0, delta, k, n, k, r, scaling, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bw_lora_merge_exact(const void* w, int64_t ldw, const void* a, const void* b, float scaling,
+                                   void* w_out, int64_t ldo, int64_t n, int64_t k, int64_t r, void* stream) {
+  using namespace bw;
+  if (int s = check_lora_args("lora_merge", a, b, n, k, r)) return s;
+  if (n == 0 || k == 0) return BW_OK;
+  if (!w || !w_out) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge: null pointer");
+  if (ldw < k || ldo < k) return fail(BW_ERR_INVALID_ARGUMENT, "lora_merge: row stride smaller than k");
+  if (int s = require_sm100()) return s;
+  return launch_lora_exact(kModeMerge, a, b, w, ldw, w_out, ldo, n, k, r, scaling, static_cast<cudaStream_t>(stream));
 }
 
 namespace bw {

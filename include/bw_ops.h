@@ -170,6 +170,18 @@ int bw_lora_delta(const void* a, const void* b, void* delta, int64_t n, int64_t 
                   float scaling, void* stream);
 
 /*
+ * Reference-order ("exact") LoRA delta and merge on the CUDA cores: each output is the reference
+ * kernels' own j-ordered fp32 accumulation (lora_ops.cu:16-27) rounded as they round it, so delta,
+ * the merged weight and a requantisation of it (bw_quantize_rowwise_int8) equal the reference
+ * pipeline bit for bit.  Same arguments as bw_lora_delta / bw_lora_merge; slower than the
+ * tensor-core path (r fp32 FMAs per output on the CUDA cores), whose sums are within one fp16 ulp.
+ */
+int bw_lora_delta_exact(const void* a, const void* b, void* delta, int64_t n, int64_t k, int64_t r,
+                        float scaling, void* stream);
+int bw_lora_merge_exact(const void* w, int64_t ldw, const void* a, const void* b, float scaling,
+                        void* w_out, int64_t ldo, int64_t n, int64_t k, int64_t r, void* stream);
+
+/*
  * In-place merge w[i] = fp16(fp32(w[i]) + fp32(delta[i])), i < numel.
  * Replaces add_delta_, src/blackwell_ops/cuda/lora_ops.cu:62-71 (kernel :32-38).
  */

@@ -232,3 +232,33 @@ def test_lora_merge_requant_many_problems_reuse_workspace(cuda_dev, ops):
         for (W, A, B, s), (q, sc) in zip(items, outs):
             qm, sm = quant.quantize_weight_int8(cuda.lora_merge(W, A, B, s).cpu().numpy(), F16)
             assert np.array_equal(q.cpu().numpy(), qm) and np.array_equal(sc.cpu().numpy(), sm)
+
+
+# exact=True: the reference's own j-ordered accumulation on the CUDA cores.  Every cfg2 projection
+# (Qwen3-0.6B, r in {16, 128}), odd shapes, strided/odd r, and a cfg5 shard (1/8 of the Llama-3-70B
+# up projection's rows): delta, merge and requantisation equal the reference pipeline bit for bit.
+EXACT_CASES = [(500 + i, r, n, k, 2.0) for i, (r, (_, k, n)) in enumerate((r, p) for r in (16, 128) for p in QWEN)] + [
+    (530, 7, 130, 200, 1.5), (531, 12, 50, 101, 2.0), (532, 128, 33, 1000, 0.75), (533, 16, 3584, 8192, 2.0)]
+
+
+@pytest.mark.parametrize("seed,r,n,k,s", EXACT_CASES)
+def test_lora_exact_mode_bit_exact(seed, r, n, k, s, cuda_dev, ops):
+    cuda, _ = ops
+    A, B, W = make(seed, r, n, k)
+    Ad, Bd, Wd = dev16(A, cuda_dev), dev16(B, cuda_dev), dev16(W, cuda_dev)
+    want_d = lora.lora_delta(A, B, s)
+    got_d = cuda.lora_delta(Ad, Bd, s, exact=True).cpu().numpy()
+    assert np.array_equal(got_d.view(np.uint16), want_d.view(np.uint16))
+    want_w = lora.add_delta(W, want_d)
+    got_w = cuda.lora_merge(Wd, Ad, Bd, s, exact=True).cpu().numpy()
+    assert np.array_equal(got_w.view(np.uint16), want_w.view(np.uint16))
+    q_want, s_want = quant.quantize_weight_int8(want_w, F16)
+    for q, sc in (cuda.lora_merge_requant(Wd, Ad, Bd, s, exact=True),
+                  cuda.lora_merge_requant_batched([(Wd, Ad, Bd, s)], exact=True)[0]):
+        assert np.array_equal(q.cpu().numpy(), q_want)
+        assert np.array_equal(sc.cpu().numpy().view(np.uint16), np.asarray(s_want).view(np.uint16))
+    # in place, strided rows of W
+    Wbig = dev16(np.concatenate([W, W[:, :8]], axis=1), cuda_dev)
+    view = Wbig[:, :k]
+    cuda.lora_merge(view, Ad, Bd, s, out=view, exact=True)
+    assert np.array_equal(view.cpu().numpy().view(np.uint16), want_w.view(np.uint16))
