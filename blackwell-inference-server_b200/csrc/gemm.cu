@@ -143,7 +143,11 @@ __device__ __forceinline__ float round_out(float v) {
 // its own accumulator; BM = 128 one.  A third issuer (warp 15, with the weight producer also
 // loading the activation tiles) measured slower on the Llama-3-70B MLP decode shapes (3.1 against
 // 4.0 TB/s): the single producer then issued one weight tile per ~1250 cycles.
-// Activation ring depth at BM = 16 (the weight ring takes the rest of 208 KB).
+// Shared memory (KB) of the two decode rings together.
+#ifndef BW_GEMM_DEC_SMEM_KB
+#define BW_GEMM_DEC_SMEM_KB 208
+#endif
+// Activation ring depth at BM = 16 (the weight ring takes the rest of the decode rings' budget).
 #ifndef BW_GEMM_XSTAGES16
 #define BW_GEMM_XSTAGES16 16
 #endif
@@ -182,7 +186,7 @@ struct PCfg {
   // k-block's weight tile; with a shallow ring its slot frees only when an MMA completes, and the
   // tile then landed a full loaded latency after the MMA was due (one stage per ~900 cycles).
   static constexpr int XSTAGES_DEC = BM == 16 ? BW_GEMM_XSTAGES16 : BM == 32 ? 12 : 5;
-  static constexpr int STAGES_DEC = (208 * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES;
+  static constexpr int STAGES_DEC = (BW_GEMM_DEC_SMEM_KB * 1024 - XSTAGES_DEC * X_BYTES) / W_BYTES;
   static constexpr int STAGES = BM < 128 ? STAGES_DEC : STAGES_PRE;
   static constexpr int XSTAGES = BM < 128 ? XSTAGES_DEC : STAGES_PRE;
   // TMEM: A buffers (64 columns each) between the dequantisers and the MMAs, as many as the
