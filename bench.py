@@ -1,7 +1,7 @@
 """Benchmark harness (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg5|cfg1|cfg2|cfg3|cfg4|quant|delta|merge] [--m M]
+                    [--workload cfg5|cfg1|cfg2|cfg3|cfg3g|cfg4|quant|delta|merge] [--m M]
 
 Workloads (synthetic seeded data, weights random-init):
 
@@ -25,6 +25,8 @@ Workloads (synthetic seeded data, weights random-init):
         rotating over 64 weight copies (> L2).  Metric GB/s.
   cfg3  decode sweep over the Qwen3-0.6B linear stack: 28 layers x 7 projections
         + LM head 1024->151936, M tokens (default 16).  Metric GB/s.
+  cfg3g  the same sweep with each layer's q/k/v and gate/up as grouped launches that
+        share their input (bw_w8a16_gemm_grouped): 4 launches per layer.  GB/s.
   cfg4  prefill W8A16 at Llama-3-8B MLP shapes (4096->14336, 14336->4096), bf16,
         M tokens (default 2048).  Metric TFLOPS.
   quant  quantize_weight_int8 of the Llama-3-8B MLP weights (bf16), GB/s.
@@ -42,6 +44,7 @@ synchronize on both sides, CUDA events on the launching stream, max over ranks.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -281,7 +284,8 @@ class MergeRequantWorkload:
 
 
 class GemmSweepWorkload:
-    """cfg1 / cfg3 / cfg4: W8A16 GEMMs through bw_w8a16_gemm on resident weights."""
+    """cfg1 / cfg3 / cfg3g / cfg4: W8A16 GEMMs through bw_w8a16_gemm (cfg3g: grouped launches through
+    bw_w8a16_gemm_grouped) on resident weights."""
 
     def __init__(self, name, dev, rank, world, m):
         from blackwell_ops import _lib
@@ -295,7 +299,7 @@ class GemmSweepWorkload:
         if name == "cfg1":
             shapes = [(1024, 3072)] * 64
             self.xdtype = torch.float16
-        elif name == "cfg3":
+        elif name in ("cfg3", "cfg3g"):
             shapes = [(k, n) for _ in range(QWEN_LAYERS) for _, k, n in QWEN] + [LM_HEAD]
             self.xdtype = torch.float16
         elif name == "cfg4":
@@ -317,17 +321,43 @@ class GemmSweepWorkload:
             self.S.append(s)
             self.X.append(randn((m, k), 1.0, self.xdtype, g, dev))
             self.Y.append(torch.empty((m, n), dtype=self.xdtype, device=dev))
-        per = [n * k + 2 * n + 2 * m * k + 2 * m * n for k, n in shapes]
+        # launches: one GEMM each, or (cfg3g) a layer's q/k/v and gate/up as grouped launches that share
+        # their input, as in a decoder layer; o, down and the LM head alone
+        if name == "cfg3g":
+            self.groups = []
+            for li in range(QWEN_LAYERS):
+                b = 7 * li
+                self.groups += [[b, b + 1, b + 2], [b + 3], [b + 4, b + 5], [b + 6]]
+            self.groups.append([len(shapes) - 1])
+            for grp in self.groups:
+                for i in grp[1:]:
+                    self.X[i] = self.X[grp[0]]  # one activation per group
+        else:
+            self.groups = [[i] for i in range(len(shapes))]
+        per = [n * k + 2 * n + 2 * m * n for k, n in shapes]
+        per = [v + (2 * m * shapes[i][0] if any(grp[0] == i for grp in self.groups) else 0) for i, v in enumerate(per)]
         fl = [2.0 * m * n * k for k, n in shapes]
         if self.rot:
             self.bytes, self.flops = per[0], fl[0]
             self.launches_per_step = 1
         else:
             self.bytes, self.flops = sum(per), sum(fl)
-            self.launches_per_step = len(shapes)
+            self.launches_per_step = len(self.groups)
         self.metric_kind = "tflops" if name == "cfg4" else "gbs"
         self.unit = "TFLOPS" if name == "cfg4" else "GB/s"
         ws = max(self.lib.bw_w8a16_gemm_workspace_size(m, n, k) for k, n in shapes)
+        self.cgroups = {}
+        for grp in self.groups:
+            if len(grp) > 1:
+                c = len(grp)
+                arr = lambda ct, vals: (ct * c)(*vals)  # noqa: E731
+                k = shapes[grp[0]][0]
+                ns = arr(ctypes.c_int64, [shapes[i][1] for i in grp])
+                self.cgroups[grp[0]] = (c, arr(ctypes.c_void_p, [self.Q[i].data_ptr() for i in grp]),
+                                        arr(ctypes.c_int64, [k] * c),
+                                        arr(ctypes.c_void_p, [self.S[i].data_ptr() for i in grp]),
+                                        arr(ctypes.c_void_p, [self.Y[i].data_ptr() for i in grp]), ns, ns, k)
+                ws = max(ws, self.lib.bw_w8a16_gemm_grouped_workspace_size(m, ns, c, k))
         self.ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
         self.xcode = 1 if self.xdtype == torch.bfloat16 else 0
 
@@ -342,13 +372,23 @@ class GemmSweepWorkload:
         if rc:
             raise RuntimeError(self.lib.bw_last_error().decode())
 
+    def _grouped(self, i, st):
+        c, w, ldw, sc, y, ldy, n, k = self.cgroups[i]
+        rc = self.lib.bw_w8a16_gemm_grouped(self.X[i].data_ptr(), self.xcode, k, c, w, ldw, sc, self.xcode, y, ldy, n,
+                                            self.m, k, self.ws.data_ptr(), self.ws.numel(), st)
+        if rc:
+            raise RuntimeError(self.lib.bw_last_error().decode())
+
     def step(self, s, st, events=None):
-        idx = [s % len(self.shapes)] if self.rot else range(len(self.shapes))
+        idx = [s % len(self.shapes)] if self.rot else [grp[0] for grp in self.groups]
         for i in idx:
             if events is not None:
                 events.append(torch.cuda.Event(enable_timing=True))
                 events[-1].record()
-            self._gemm(i, st)
+            if i in self.cgroups:
+                self._grouped(i, st)
+            else:
+                self._gemm(i, st)
             if events is not None:
                 events.append(torch.cuda.Event(enable_timing=True))
                 events[-1].record()
@@ -358,16 +398,21 @@ class GemmSweepWorkload:
         self.hX = [torch.randn(x.shape, generator=g).to(self.xdtype).pin_memory() for x in self.X]
         self.hY = [torch.empty(y.shape, dtype=self.xdtype).pin_memory() for y in self.Y]
         idx = [0] if self.rot else range(len(self.shapes))
-        self.h2d = sum(self.hX[i].numel() * 2 for i in idx)
+        self.h2d = sum(self.hX[i].numel() * 2 for i in idx if any(grp[0] == i for grp in self.groups))
         self.d2h = sum(self.hY[i].numel() * 2 for i in idx)
 
     def e2e_step(self, s):
-        from blackwell_ops.kernels import int8_gemm
+        from blackwell_ops.kernels import int8_gemm, int8_gemm_grouped
 
-        idx = [s % len(self.shapes)] if self.rot else range(len(self.shapes))
-        for i in idx:
-            x = self.hX[i].to(self.dev, non_blocking=True)
-            self.hY[i].copy_(int8_gemm(x, self.Q[i], self.S[i]), non_blocking=True)
+        groups = [[s % len(self.shapes)]] if self.rot else self.groups
+        for grp in groups:
+            x = self.hX[grp[0]].to(self.dev, non_blocking=True)
+            if len(grp) == 1:
+                ys = [int8_gemm(x, self.Q[grp[0]], self.S[grp[0]])]
+            else:
+                ys = int8_gemm_grouped(x, [(self.Q[i], self.S[i]) for i in grp])
+            for i, y in zip(grp, ys):
+                self.hY[i].copy_(y, non_blocking=True)
 
     def cpu_sample(self, step_index: int):
         from oracle import torch_port
@@ -678,8 +723,8 @@ class NSplitWorkload:
 def make_workload(args, dev, rank, world):
     if args.workload == "cfg2":
         return MergeRequantWorkload(dev, rank, world)
-    if args.workload in ("cfg1", "cfg3", "cfg4"):
-        m = args.m if args.m else {"cfg1": 16, "cfg3": 16, "cfg4": 2048}[args.workload]
+    if args.workload in ("cfg1", "cfg3", "cfg3g", "cfg4"):
+        m = args.m if args.m else {"cfg1": 16, "cfg3": 16, "cfg3g": 16, "cfg4": 2048}[args.workload]
         return GemmSweepWorkload(args.workload, dev, rank, world, m)
     if args.workload == "quant":
         return QuantizeWorkload(dev, rank, world)
@@ -768,7 +813,7 @@ class GemmCpuShim:
         self.xdtype = torch.bfloat16 if self.name == "cfg4" else torch.float16
         if self.name == "cfg1":
             self.shapes = [(1024, 3072)]
-        elif self.name == "cfg3":
+        elif self.name in ("cfg3", "cfg3g"):
             self.shapes = [(k, n) for _, k, n in QWEN] + [LM_HEAD]
         elif self.name == "cfg5":
             self.shapes = list(LLAMA70B_MLP)
@@ -784,7 +829,7 @@ class GemmCpuShim:
 
 METRIC = "W8A16 GEMM HBM GB/s (decode) / TFLOPS (prefill, ΔW) vs B200 roofline"
 
-DEFAULT_M = {"cfg1": 16, "cfg3": 16, "cfg4": 2048, "cfg5": 16}
+DEFAULT_M = {"cfg1": 16, "cfg3": 16, "cfg3g": 16, "cfg4": 2048, "cfg5": 16}
 
 
 def workload_config(name: str, m: int) -> dict:
@@ -801,6 +846,8 @@ def workload_config(name: str, m: int) -> dict:
     desc = {"cfg1": "cfg1: W8A16 GEMM X[16,1024] x W[3072,1024]^T, fp16; one step = 64 GEMMs on 64 distinct "
                     "weight copies (210 MB > L2)",
             "cfg3": f"cfg3: Qwen3-0.6B decode sweep, 28 layers x 7 projections + LM head, M={m}, fp16",
+            "cfg3g": f"cfg3g: the cfg3 sweep with each layer's q/k/v and gate/up as grouped launches sharing their "
+                     f"input (4 launches per layer), M={m}, fp16",
             "cfg4": f"cfg4: Llama-3-8B MLP prefill W8A16 (4096->14336, 14336->4096), M={m}, bf16",
             "cfg5": f"cfg5: Llama-3-70B MLP W8A16 (8192->28672, 28672->8192), 32 adapter int8 copies "
                     f"(r in {{16,64,128}}), M={m}, bf16"}[name]

@@ -54,6 +54,9 @@ SIGNATURES = {
     "bw_w8a16_gemm_static_scratch_bytes": (_c.c_size_t, []),
     "bw_w8a16_gemm_noalloc": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,
                                          _P]),
+    "bw_w8a16_gemm_grouped_workspace_size": (_c.c_size_t, [_I64, _P, _c.c_int, _I64]),
+    "bw_w8a16_gemm_grouped": (_c.c_int, [_P, _c.c_int, _I64, _c.c_int, _P, _P, _P, _c.c_int, _P, _P, _P, _I64, _I64,
+                                         _P, _c.c_size_t, _P]),
     "bw_w8a16_gemm_allgather_workspace_size": (_c.c_size_t, [_I64, _I64, _I64]),
     "bw_w8a16_gemm_allgather_signal_bytes": (_c.c_size_t, [_I64, _I64, _c.c_int]),
     "bw_w8a16_gemm_allgather": (_c.c_int, [_P, _c.c_int, _I64, _P, _I64, _P, _c.c_int, _P, _I64, _I64, _I64, _I64,

@@ -178,6 +178,55 @@ def int8_gemm_swiglu(x: torch.Tensor, w_gate: torch.Tensor, s_gate: torch.Tensor
     return y
 
 
+def int8_gemm_grouped(x: torch.Tensor, weights) -> list[torch.Tensor]:
+    """``[int8_gemm(x, w_i, s_i) for (w_i, s_i) in weights]`` in one launch (up to 4 GEMMs sharing x,
+    e.g. a layer's q/k/v or gate/up projections): the persistent kernel's schedule spans the union of
+    their output tiles, so the small projections stream as one weight walk.  Each result meets the
+    int8_gemm tolerance; split-K pieces may be summed in another grouping than in separate calls.
+    """
+    import ctypes
+
+    weights = [(w, s) for w, s in weights]
+    if not 1 <= len(weights) <= 4:
+        raise RuntimeError("int8_gemm_grouped: 1 to 4 (w_int8, scale) pairs")
+    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16) or x.dim() != 2:
+        raise RuntimeError("int8_gemm_grouped: x must be a 2-D fp16 / bf16 CUDA tensor")
+    M, K = x.shape
+    sdt = weights[0][1].dtype
+    ws_, ss, ys = [], [], []
+    for w, s in weights:
+        if not (w.is_cuda and s.is_cuda) or w.dtype != torch.int8 or w.dim() != 2 or w.shape[1] != K:
+            raise RuntimeError("int8_gemm_grouped: every w_int8 must be a CUDA int8 [N, K] tensor with x's K")
+        if s.dtype != sdt or s.dtype not in DTYPE_CODE or s.numel() != w.shape[0]:
+            raise RuntimeError("int8_gemm_grouped: scales must share one dtype and have N elements")
+        ws_.append(w if w.stride(1) == 1 and w.stride(0) >= K else w.contiguous())
+        ss.append(s.reshape(-1).contiguous())
+        ys.append(torch.empty(M, w.shape[0], device=x.device, dtype=x.dtype))
+    if M == 0 or K == 0 or any(w.shape[0] == 0 for w in ws_):
+        return [int8_gemm(x, w, s) for w, s in weights]
+    if x.stride(1) != 1 or x.stride(0) < K:
+        x = x.contiguous()
+    c = len(ws_)
+
+    def ptrs(ts):
+        return (ctypes.c_void_p * c)(*[t.data_ptr() for t in ts])
+
+    def i64(vals):
+        return (ctypes.c_int64 * c)(*vals)
+
+    n = i64([w.shape[0] for w in ws_])
+    with torch.cuda.device(x.device):
+        st = stream_ptr(x.device)
+        nbytes = lib.bw_w8a16_gemm_grouped_workspace_size(M, n, c, K)
+        wsp = _workspace(x.device, st, nbytes)
+        check(lib.bw_w8a16_gemm_grouped(x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0), c, ptrs(ws_),
+                                        i64([w.stride(0) for w in ws_]), ptrs(ss), DTYPE_CODE[sdt], ptrs(ys),
+                                        i64([y.shape[1] for y in ys]), n, M, K,
+                                        wsp.data_ptr() if wsp is not None else None,
+                                        wsp.numel() if wsp is not None else 0, st), "int8_gemm_grouped")
+    return ys
+
+
 def int8_gemm_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, norm_weight: torch.Tensor,
                       w_int8: torch.Tensor, scale: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """``int8_gemm(fused_residual_rmsnorm(x, residual, norm_weight, eps), w_int8, scale)`` in one call.

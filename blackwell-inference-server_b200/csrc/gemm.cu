@@ -18,6 +18,7 @@
 // multiples of 16 bytes) go to a CUDA-core kernel with the same arithmetic.
 #include <stdio.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 
@@ -70,6 +71,25 @@ constexpr int kGatherMaxM = 256;  // largest M of the fused all-gather (the mail
 __host__ __device__ inline size_t gather_pad_bytes(long long m, long long n, int world) {
   const long long rowwords = (n + 127) / 128 * 64;
   return kMailbox0 + static_cast<size_t>(2) * world * m * rowwords * 8;
+}
+
+// Grouped launch: up to kMaxGroup GEMMs that share x (same M, K, dtypes), e.g. the q/k/v or
+// gate/up projections of a layer, as one schedule over the union of their n-tiles.  Problem p owns
+// n-tiles [tile0[p], tile0[p+1]); count == 0 is a single GEMM (the kernel's own tm_w, scale, y).
+constexpr int kMaxGroup = 4;
+struct GroupArgs {
+  CUtensorMap w[kMaxGroup];
+  unsigned long long scale[kMaxGroup], y[kMaxGroup];
+  long long ldy[kMaxGroup];
+  int n[kMaxGroup];
+  int tile0[kMaxGroup + 1];
+  int count;
+};
+
+__device__ __forceinline__ int group_of(const GroupArgs& grp, int nt) {
+  int p = 0;
+  while (p + 1 < grp.count && nt >= grp.tile0[p + 1]) ++p;
+  return p;
 }
 
 // 8 consecutive outputs of one token row, already rounded, as one 16-byte store.
@@ -329,10 +349,10 @@ enum PersistentWaitSite : int {
 template <int BM, bool BF16, bool GLU>
 __global__ void __launch_bounds__(512, 1)
     w8a16_persistent_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
-                            const __grid_constant__ CUtensorMap tm_x, const void* __restrict__ scale,
-                            const void* __restrict__ scale2, int sdtype, void* __restrict__ y, int64_t ldy, int M,
-                            int N, const Sched sc, float* __restrict__ ws, int* __restrict__ counters,
-                            const GatherArgs g) {
+                            const __grid_constant__ CUtensorMap tm_x, const void* __restrict__ scale_in,
+                            const void* __restrict__ scale2, int sdtype, void* __restrict__ y_in, int64_t ldy_in,
+                            int M, int N_in, const Sched sc, float* __restrict__ ws, int* __restrict__ counters,
+                            const GatherArgs g, const __grid_constant__ GroupArgs grp) {
   using C = PCfg<BM>;
   constexpr int STAGES = C::STAGES;
   constexpr int XSTAGES = C::XSTAGES;
@@ -389,6 +409,7 @@ __global__ void __launch_bounds__(512, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
+    for (int pg = 0; pg < grp.count; ++pg) tma_prefetch_desc(&grp.w[pg]);
     if (GLU) tma_prefetch_desc(&tm_w2);
     tma_prefetch_desc(&tm_x);
   }
@@ -439,7 +460,14 @@ __global__ void __launch_bounds__(512, 1)
             tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 64, pol_w);
             tma_load_2d(sW + s * C::W_BYTES + C::W_BYTES / 2, &tm_w2, &full[s], (sg.k0 + i) * C::BK, nt * 64, pol_w);
           } else {
-            tma_load_2d(sW + s * C::W_BYTES, &tm_w, &full[s], (sg.k0 + i) * C::BK, nt * 128, pol_w);
+            const CUtensorMap* wm = &tm_w;
+            int wrow = nt * 128;
+            if (grp.count > 0) {  // grouped launch: the tile's problem and its rows there
+              const int pg = group_of(grp, nt);
+              wm = &grp.w[pg];
+              wrow = (nt - grp.tile0[pg]) * 128;
+            }
+            tma_load_2d(sW + s * C::W_BYTES, wm, &full[s], (sg.k0 + i) * C::BK, wrow, pol_w);
           }
         }
       }
@@ -664,8 +692,22 @@ __global__ void __launch_bounds__(512, 1)
     Seg sg;
     for (; wk.next(sc, sg); it0 += sg.nkb, ++j) {
       const int t = sg.t;
-      const int nt = t / sc.m_tiles;
-      const int mt = t - nt * sc.m_tiles;
+      const int nt_all = t / sc.m_tiles;
+      const int mt = t - nt_all * sc.m_tiles;
+      // the tile's GEMM (a grouped launch holds several) and its n-tile there
+      int nt = nt_all;
+      const void* scale = scale_in;
+      void* y = y_in;
+      int64_t ldy = ldy_in;
+      int N = N_in;
+      if (grp.count > 0) {
+        const int pg = group_of(grp, nt_all);
+        nt = nt_all - grp.tile0[pg];
+        scale = reinterpret_cast<const void*>(grp.scale[pg]);
+        y = reinterpret_cast<void*>(grp.y[pg]);
+        ldy = grp.ldy[pg];
+        N = grp.n[pg];
+      }
       // issuer h holds part of this segment iff one of its k-blocks (it % NI == h) lies in it
       auto has = [&](int h) { return sg.nkb >= NI || (h - it0 % NI + NI) % NI < sg.nkb; };
       const int n = GLU ? nt * 64 + (row & 63) : nt * 128 + row;
@@ -892,8 +934,21 @@ __global__ void __launch_bounds__(512, 1)
         for (int i = 0; i < npend; ++i) {
           const int t = pend[1 + 4 * i], n_parts = pend[2 + 4 * i], c_first = pend[3 + 4 * i];
           const size_t poff0 = static_cast<size_t>(pend[4 + 4 * i]);
-          const int nt = t / sc.m_tiles;
-          const int m0 = (t - nt * sc.m_tiles) * BM;
+          const int nt_all = t / sc.m_tiles;
+          const int m0 = (t - nt_all * sc.m_tiles) * BM;
+          int nt = nt_all;
+          const void* scale = scale_in;
+          void* y = y_in;
+          int64_t ldy = ldy_in;
+          int N = N_in;
+          if (grp.count > 0) {
+            const int pg = group_of(grp, nt_all);
+            nt = nt_all - grp.tile0[pg];
+            scale = reinterpret_cast<const void*>(grp.scale[pg]);
+            y = reinterpret_cast<void*>(grp.y[pg]);
+            ldy = grp.ldy[pg];
+            N = grp.n[pg];
+          }
           const float* base = ws + static_cast<size_t>(c_first) * 2 * kPiece;
           __threadfence();  // the contributors' pieces, published before their tickets
           for (int f = tid; f < 32 * BM; f += C::THREADS) {
@@ -972,7 +1027,7 @@ __global__ void __launch_bounds__(512, 1)
             const int rows = min(BM, M - mt * BM);
             const uint64_t* src =
                 mbox + (static_cast<size_t>((ep & 1u) * g.world + p) * M + mt * BM) * g.rowwords + nt * 64;
-            uint16_t* dst = reinterpret_cast<uint16_t*>(g.ybase) + static_cast<int64_t>(mt * BM) * ldy +
+            uint16_t* dst = reinterpret_cast<uint16_t*>(g.ybase) + static_cast<int64_t>(mt * BM) * ldy_in +
                             static_cast<int64_t>(p) * g.n + nt * 128;
             const int cols = min(128, g.n - nt * 128);
             // 2 words (4 outputs) per thread per load, four loads in flight
@@ -1000,7 +1055,7 @@ __global__ void __launch_bounds__(512, 1)
                 if (!ok) break;
                 // 4 outputs: token w / 64, columns 2 (w % 64) .. + 3 of the tile
                 const int c = 2 * (w & 63);
-                uint16_t* d = dst + static_cast<int64_t>(w >> 6) * ldy + c;
+                uint16_t* d = dst + static_cast<int64_t>(w >> 6) * ldy_in + c;
                 const uint32_t lo = static_cast<uint32_t>(v[i][0]), hi = static_cast<uint32_t>(v[i][1]);
                 if (g.vec4 && c + 4 <= cols) {
                   *reinterpret_cast<uint2*>(d) = make_uint2(lo, hi);
@@ -1181,7 +1236,7 @@ static bool g_use_pdl = true;
 template <int BM, bool BF16, bool GLU>
 static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tw2, const CUtensorMap& tx,
                              const void* scale, const void* scale2, int sdt, void* y, int64_t ldy, int M, int N,
-                             float* ws, int* counters, const GatherArgs& g, cudaStream_t st) {
+                             float* ws, int* counters, const GatherArgs& g, const GroupArgs& grp, cudaStream_t st) {
   using C = PCfg<BM>;
   static std::once_flag once[64];
   int dev = 0;
@@ -1212,24 +1267,30 @@ static int launch_persistent(const GemmPlan& p, const CUtensorMap& tw, const CUt
   sc.units = p.units;
   sc.work = p.work;
   return check_cuda(cudaLaunchKernelEx(&cfg, w8a16_persistent_kernel<BM, BF16, GLU>, tw, tw2, tx, scale, scale2, sdt,
-                                       y, ldy, M, N, sc, ws, counters, g),
+                                       y, ldy, M, N, sc, ws, counters, g, grp),
                     "cudaLaunchKernelEx(w8a16_persistent_kernel)");
 }
 
 template <bool BF16, bool GLU>
 static int dispatch_gemm(const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap& tw2, const CUtensorMap& tx,
                          const void* scale, const void* scale2, int sdt, void* y, int64_t ldy, int M, int N, float* ws,
-                         int* counters, const GatherArgs& g, cudaStream_t st) {
+                         int* counters, const GatherArgs& g, const GroupArgs& grp, cudaStream_t st) {
   switch (p.bm) {
     case 16:
-      return launch_persistent<16, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
+      return launch_persistent<16, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, grp, st);
     case 32:
-      return launch_persistent<32, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
+      return launch_persistent<32, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, grp, st);
     case 64:
-      return launch_persistent<64, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
+      return launch_persistent<64, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, grp, st);
     default:
-      return launch_persistent<128, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, st);
+      return launch_persistent<128, BF16, GLU>(p, tw, tw2, tx, scale, scale2, sdt, y, ldy, M, N, ws, counters, g, grp,
+                                               st);
   }
+}
+
+static const GroupArgs& no_group() {
+  static const GroupArgs z = {};
+  return z;
 }
 
 static bool tma_ok(const void* p, int64_t ld_bytes) {
@@ -1260,7 +1321,7 @@ namespace bw {
 static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
                      int scale_dtype, void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace,
                      size_t workspace_bytes, const GatherArgs& g, void* stream, const int8_t* w2 = nullptr,
-                     const void* scale2 = nullptr) {
+                     const void* scale2 = nullptr, const GroupArgs* grp = nullptr) {
   const bool glu = w2 != nullptr;
   if (m < 0 || n < 0 || k < 1)
     return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: need m, n >= 0 and k >= 1 (got %lld, %lld, %lld)",
@@ -1273,7 +1334,8 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
   if (!x || !w || !scale || !y) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: null pointer");
   if (glu && !scale2) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm_swiglu: null pointer");
   if (glu && g.world > 0) return fail(BW_ERR_UNSUPPORTED, "int8_gemm_swiglu: no all-gather variant");
-  if (ldx < k || ldw < k || ldy < n) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: row stride too small");
+  if (ldx < k || ldw < k || (grp == nullptr && ldy < n))
+    return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: row stride too small");
   if (m > (1LL << 30) || n > (1LL << 30) || k > (1LL << 30))
     return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm: dimension too large");
   if (int s = require_sm100()) return s;
@@ -1318,9 +1380,12 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
     ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.counter_bytes);
   }
   CUtensorMap tw, tw2, tx;
-  if (int s = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k, ldw, glu ? 64 : 128, 128,
-                           CU_TENSOR_MAP_SWIZZLE_128B))
+  if (grp != nullptr) {
+    tw = grp->w[0];  // the grouped kernel reads its problems' maps; this one is not used
+  } else if (int s = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k, ldw, glu ? 64 : 128, 128,
+                                  CU_TENSOR_MAP_SWIZZLE_128B)) {
     return s;
+  }
   if (glu) {
     if (int s = make_tmap_2d(&tw2, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k, ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
       return s;
@@ -1333,15 +1398,16 @@ static int gemm_impl(const void* x, int x_dtype, int64_t ldx, const int8_t* w, i
   if (glu) {
     if (bf16)
       return dispatch_gemm<true, true>(p, tw, tw2, tx, scale, scale2, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
-                                       g, st);
+                                       g, no_group(), st);
     return dispatch_gemm<false, true>(p, tw, tw2, tx, scale, scale2, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
-                                      g, st);
+                                      g, no_group(), st);
   }
+  const GroupArgs& ga = grp != nullptr ? *grp : no_group();
   if (bf16)
     return dispatch_gemm<true, false>(p, tw, tw2, tx, scale, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
-                                      g, st);
+                                      g, ga, st);
   return dispatch_gemm<false, false>(p, tw, tw2, tx, scale, scale, scale_dtype, y, ldy, (int)m, (int)n, ws, counters,
-                                     g, st);
+                                     g, ga, st);
 }
 }  // namespace bw
 
@@ -1352,6 +1418,78 @@ extern "C" int bw_w8a16_gemm(const void* x, int x_dtype, int64_t ldx, const int8
   g.vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && ldy % 8 == 0;
   return bw::gemm_impl(x, x_dtype, ldx, w, ldw, scale, scale_dtype, y, ldy, m, n, k, workspace, workspace_bytes, g,
                        stream);
+}
+
+// Grouped W8A16 GEMM: up to kMaxGroup GEMMs sharing x (y_i = x @ (w_i * scale_i)^T, e.g. the q/k/v
+// projections of a layer) in one persistent launch over the union of their tiles.
+namespace bw {
+static bool group_shape_ok(const int64_t* n, int count, int64_t* tiles) {
+  if (count < 1 || count > kMaxGroup || n == nullptr) return false;
+  int64_t t = 0;
+  for (int i = 0; i < count; ++i) {
+    if (n[i] < 1 || n[i] > (1LL << 30)) return false;
+    t += (n[i] + 127) / 128;
+  }
+  *tiles = t;
+  return true;
+}
+}  // namespace bw
+
+extern "C" size_t bw_w8a16_gemm_grouped_workspace_size(int64_t m, const int64_t* n, int count, int64_t k) {
+  int64_t tiles = 0;
+  if (m <= 0 || k <= 0 || !bw::group_shape_ok(n, count, &tiles)) return 0;
+  // the union's plan, or (layouts TMA cannot address) the largest single GEMM's
+  size_t need = bw_w8a16_gemm_workspace_size(m, 128 * tiles, k);
+  for (int i = 0; i < count; ++i) need = std::max(need, bw_w8a16_gemm_workspace_size(m, n[i], k));
+  return need;
+}
+
+extern "C" int bw_w8a16_gemm_grouped(const void* x, int x_dtype, int64_t ldx, int count, const int8_t* const* w,
+                                     const int64_t* ldw, const void* const* scale, int scale_dtype, void* const* y,
+                                     const int64_t* ldy, const int64_t* n, int64_t m, int64_t k, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  using namespace bw;
+  int64_t tiles = 0;
+  if (!group_shape_ok(n, count, &tiles) || !w || !ldw || !scale || !y || !ldy)
+    return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm_grouped: need 1..%d problems with n >= 1 and their arrays",
+                kMaxGroup);
+  if (m < 0 || k < 1) return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm_grouped: need m >= 0 and k >= 1");
+  for (int i = 0; i < count; ++i) {
+    if (!w[i] || !scale[i] || !y[i])
+      return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm_grouped: null pointer (problem %d)", i);
+    if (ldw[i] < k || ldy[i] < n[i])
+      return fail(BW_ERR_INVALID_ARGUMENT, "int8_gemm_grouped: row stride too small (problem %d)", i);
+  }
+  if (m == 0) return BW_OK;
+  bool tma = tma_ok(x, ldx * 2);
+  for (int i = 0; i < count; ++i) tma = tma && tma_ok(w[i], ldw[i]);
+  if (!tma || count == 1) {  // one launch per GEMM (each picks its own path)
+    for (int i = 0; i < count; ++i)
+      if (int s = bw_w8a16_gemm(x, x_dtype, ldx, w[i], ldw[i], scale[i], scale_dtype, y[i], ldy[i], m, n[i], k,
+                                workspace, workspace_bytes, stream))
+        return s;
+    return BW_OK;
+  }
+  GroupArgs ga = {};
+  ga.count = count;
+  GatherArgs g = {};
+  g.vec = 1;
+  int t0 = 0;
+  for (int i = 0; i < count; ++i) {
+    if (int s = make_tmap_2d(&ga.w[i], w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, n[i], k, ldw[i], 128, 128,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return s;
+    ga.scale[i] = reinterpret_cast<unsigned long long>(scale[i]);
+    ga.y[i] = reinterpret_cast<unsigned long long>(y[i]);
+    ga.ldy[i] = ldy[i];
+    ga.n[i] = static_cast<int>(n[i]);
+    ga.tile0[i] = t0;
+    t0 += static_cast<int>((n[i] + 127) / 128);
+    g.vec &= reinterpret_cast<uintptr_t>(y[i]) % 16 == 0 && ldy[i] % 8 == 0;
+  }
+  ga.tile0[count] = t0;
+  return gemm_impl(x, x_dtype, ldx, w[0], ldw[0], scale[0], scale_dtype, y[0], ldy[0], m, 128 * tiles, k, workspace,
+                   workspace_bytes, g, stream, nullptr, nullptr, &ga);
 }
 
 extern "C" size_t bw_w8a16_gemm_swiglu_workspace_size(int64_t m, int64_t n, int64_t k) {

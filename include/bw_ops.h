@@ -115,6 +115,21 @@ int bw_w8a16_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, const int8_t*
                           int64_t n, int64_t k, void* stream);
 
 /*
+ * Grouped W8A16 GEMM: y_i = x @ (w_i * scale_i)^T for count <= 4 GEMMs that share x [m, k]
+ * (e.g. a layer's q/k/v or gate/up projections), in one persistent launch whose schedule spans
+ * the union of their output tiles, so small projections stream as one weight walk instead of one
+ * latency-bound launch each.  w_i [n_i, k] int8 (row stride ldw[i]), scale_i [n_i] (scale_dtype for
+ * all), y_i [m, ldy[i]] in x's dtype.  Workspace: bw_w8a16_gemm_grouped_workspace_size bytes, its
+ * first 4 KB zero, as for bw_w8a16_gemm.  Layouts TMA cannot address run as separate bw_w8a16_gemm
+ * calls.  No reference counterpart (the reference calls int8_gemm once per projection).
+ */
+size_t bw_w8a16_gemm_grouped_workspace_size(int64_t m, const int64_t* n, int count, int64_t k);
+int bw_w8a16_gemm_grouped(const void* x, int x_dtype, int64_t ldx, int count, const int8_t* const* w,
+                          const int64_t* ldw, const void* const* scale, int scale_dtype, void* const* y,
+                          const int64_t* ldy, const int64_t* n, int64_t m, int64_t k, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/*
  * Column-parallel N-split W8A16 GEMM with the all-gather fused into the
  * epilogue (the north star's N-split; the reference has no multi-GPU path).
  * Rank `rank` of `world` (<= 8) holds w rows [0, n) of its shard; rank p's
