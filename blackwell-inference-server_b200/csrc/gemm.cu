@@ -126,27 +126,28 @@ __device__ __forceinline__ float round_out(float v) {
 // ---------------------------------------------------------------------------
 // Persistent W8A16 GEMM for every M (decode, prefill).
 //
-// One CTA per SM walks work units (m_tile fastest, then n_tile, then k-split)
-// with a stride of gridDim.x; the TMA producer streams W/x stages continuously
-// across units, so the weight stream never drains between tiles, and the units
-// that share a weight tile run side by side (one DRAM read, the rest from L2).
+// One CTA per SM walks its work (split-K units b, b + grid, ... or one contiguous stream-K range
+// of the tiles' k-blocks laid end to end); the TMA producers stream W/x stages continuously
+// across units, so the weight stream never drains between tiles.
 // 512 threads:
-//   warp 0       TMA producer of the weight tiles (STAGES-deep ring, 128 x 128 B)
-//   warp 15      TMA producer of the activation tiles (BM x 128 per stage)
+//   warp 0       TMA producer of the weight tiles (STAGES-deep ring, 128 x 128 B boxes, requested
+//                BW_GEMM_W_GROUP k-blocks at a time)
+//   warp 15      TMA producer of the activation tiles (their own XSTAGES-deep ring)
 //   warp 1       TMEM owner (512 columns) + tcgen05.mma issuer 0
 //   warp 14      tcgen05.mma issuer 1 (BM <= 64)
 //   warps 2-9    dequantisers in two groups of four that take alternate k-blocks
 //                (thread = weight row, all 128 columns of the stage); int8 ->
-//                f16/bf16 straight into a TMEM A buffer (tcgen05.st), 4 x 64 cols
+//                f16/bf16 straight into a TMEM A buffer (tcgen05.st), up to six of 64 columns
 //   warps 10-13  epilogue
 // The MMA is the TS form: A (dequantised W) from TMEM, B (x) from shared memory.
-// A weight slot is released as soon as a dequantiser group has read it into
-// registers, before that group waits for a free TMEM buffer, and an x slot when
-// the MMAs that read it complete, so the weight ring stays full of loads in
-// flight.  With two issuers, issuer h issues the K=16 slices [4h, 4h+4) of every
-// k-block into its own accumulator and the epilogue adds the two (a fixed order,
-// so the result does not depend on timing).  Accumulators are double-buffered
-// (DBUF = 2), so a tile's epilogue overlaps the next tile's mainloop.
+// A weight slot is released as soon as a dequantiser group has the row in registers, before it
+// converts and waits for a free TMEM buffer, and an x slot when the MMAs that read it complete,
+// so the weight ring stays full of loads in flight.  With two issuers, issuer h takes every other
+// k-block into its own accumulator and the epilogue adds the two in issuer order (a fixed order,
+// so the result does not depend on timing).  Accumulators are double-buffered (DBUF = 2), so a
+// tile's epilogue overlaps the next tile's mainloop.  After the main loop all 512 threads sum the
+// stream-K tiles this CTA finished last and, for the all-gather, receive the peers' tiles.
+// A grouped launch (GroupArgs) runs up to four GEMMs that share x over the union of their tiles.
 // Programmatic dependent launch: the weight producer never waits for the
 // preceding kernel (weights do not depend on it); the activation producer and
 // the epilogue wait (griddepcontrol.wait) before their first global access.
