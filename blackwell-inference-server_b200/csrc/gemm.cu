@@ -177,6 +177,9 @@ __device__ __forceinline__ float round_out(float v) {
 #ifndef BW_GEMM_W_GROUP
 #define BW_GEMM_W_GROUP 4
 #endif
+#ifndef BW_GEMM_W_GROUP_PRE  // the same for prefill tiles (BM = 128)
+#define BW_GEMM_W_GROUP_PRE 1
+#endif
 // Loads in flight per thread in the deferred stream-K reduction (a tile cut into up to ~20
 // pieces at small per-rank N).
 #ifndef BW_GEMM_RED_BATCH
@@ -443,10 +446,11 @@ __global__ void __launch_bounds__(512, 1)
         const int nt = sg.t / sc.m_tiles;
         for (int i = 0; i < sg.nkb; ++i, ++it) {
           const int s = it % STAGES;
-          if constexpr (BW_GEMM_W_GROUP > 1 && BM < 128) {
+          constexpr int WG = BM < 128 ? BW_GEMM_W_GROUP : BW_GEMM_W_GROUP_PRE;
+          if constexpr (WG > 1) {
             // wait for the group's last slot before issuing its first k-block (each slot's own wait follows)
-            const int jl = it + min(BW_GEMM_W_GROUP, sg.nkb - i) - 1;
-            if (i % BW_GEMM_W_GROUP == 0 && jl >= STAGES &&
+            const int jl = it + min(WG, sg.nkb - i) - 1;
+            if (i % WG == 0 && jl >= STAGES &&
                 !mbar_wait(&empty[jl % STAGES], ((jl / STAGES) & 1) ^ 1, abort_flag, kSitePProd)) {
               ok = false;
               break;
