@@ -163,7 +163,7 @@ __device__ __forceinline__ float round_out(float v) {
 // Decode tiles (BM <= 64) run two issuers (warps 1, 14), each taking every other k-block into
 // its own accumulator; BM = 128 one.  A third issuer (warp 15, with the weight producer also
 // loading the activation tiles) measured slower on the Llama-3-70B MLP decode shapes (3.1 against
-// 4.0 TB/s): the single producer then issued one weight tile per ~1250 cycles.
+// 4.0 TB/s; the single producer then issued one weight tile per ~1250 cycles) and is not kept.
 // Shared memory (KB) of the two decode rings together.
 #ifndef BW_GEMM_DEC_SMEM_KB
 #define BW_GEMM_DEC_SMEM_KB 208
@@ -185,9 +185,6 @@ __device__ __forceinline__ float round_out(float v) {
 #ifndef BW_GEMM_RED_BATCH
 #define BW_GEMM_RED_BATCH 12
 #endif
-#ifndef BW_GEMM_DEC_ISSUERS
-#define BW_GEMM_DEC_ISSUERS 2
-#endif
 template <int BM>
 struct PCfg {
   static constexpr int BK = 128;
@@ -195,10 +192,7 @@ struct PCfg {
   static constexpr int X_PANEL = BM * 128;
   static constexpr int X_BYTES = 2 * X_PANEL;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int NI = BM <= 32 ? BW_GEMM_DEC_ISSUERS : BM == 64 ? 2 : 1;
-  // with three issuers warp 15 is an issuer and each issuer loads the activation tiles of its own
-  // k-blocks ahead of its MMAs (else warp 15 loads them all)
-  static constexpr bool ISSUER_X = NI >= 3;
+  static constexpr int NI = BM <= 64 ? 2 : 1;
   // Prefill ring: weight + activation tiles per stage, up to 4 stages of 48 KB.
   static constexpr int STAGES_PRE = (220 * 1024) / STAGE_BYTES > 8 ? 8 : (220 * 1024) / STAGE_BYTES;
   // Decode rings.  The weight stream is bound by the bytes a CTA keeps in flight (Little's law:
@@ -229,11 +223,10 @@ struct PCfg {
   static constexpr int SMEM = OFF_XCH + 4096 + 1024;
   static constexpr int THREADS = 512;
   static_assert(BM >= 16 && BM <= 128 && BM % 16 == 0, "UMMA N for M=128");
-  static_assert(NI >= 1 && NI <= 3, "one to three MMA issuers");
+  static_assert(NI >= 1 && NI <= 2, "one or two MMA issuers");
   static_assert(ASTAGES >= 2, "TMEM A buffers");
   static_assert(D_COL0 + DBUF * NI * BM <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(!ISSUER_X || XSTAGES >= 2 * NI, "activation ring too shallow for the issuers' look-ahead");
   // barriers, then 32 bytes of slots (TMEM address, abort flag, ticket, epoch, trace record) and the
   // deferred-reduction list (count + two entries of four ints)
   static_assert((2 * STAGES + 2 * XSTAGES + 2 * ASTAGES + 4 + 1) * 8 + 32 + 48 <= BAR_BYTES, "barrier area");
@@ -480,7 +473,7 @@ __global__ void __launch_bounds__(512, 1)
         for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
           mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, kSitePDrain);
     }
-  } else if (warp == 15 && !C::ISSUER_X) {
+  } else if (warp == 15) {
     // ---------------- TMA producer: activation tiles (after the predecessor) ----------------
     if (lane == 0) {
       const uint64_t pol_x = l2_policy_evict_last();
@@ -507,48 +500,18 @@ __global__ void __launch_bounds__(512, 1)
         for (int j = (it > XSTAGES ? it - XSTAGES : 0); j < it; ++j)
           mbar_wait(&xfull[j % XSTAGES], (j / XSTAGES) & 1, nullptr, kSitePDrain);
     }
-  } else if (warp == 1 || (NI >= 2 && warp == 14) || (NI >= 3 && warp == 15)) {
+  } else if (warp == 1 || (NI >= 2 && warp == 14)) {
     // ---------------- MMA issuers ----------------
     if (lane == 0) {
       // Issuer h takes the k-blocks it with it % NI == h, all eight K=16 slices of each, into
       // its own accumulator, so the issuers' MMA streams, waits and commits run side by side.
       // The epilogue adds the accumulators in a fixed order.
       constexpr uint32_t idesc = make_idesc_f16(128, BM, BF16, false);
-      const int h = warp == 1 ? 0 : warp == 14 ? 1 : 2;  // issuer index
+      const int h = warp == 1 ? 0 : 1;  // issuer index
       int it = 0, j = 0;
       bool ok = true;
       SegWalk wk(sc, blockIdx.x, gridDim.x);
       Seg sg;
-      // ISSUER_X: this issuer's activation tiles (k-blocks jx = h, h + NI, ...), loaded ahead of its
-      // MMAs; a slot is refilled once the MMAs of the k-block that last used it have completed.
-      int jx = h, xbase = 0, xcons = h;  // xcons: this issuer's next k-block whose tile it has not waited for
-      bool xseg = false;
-      SegWalk wx(sc, blockIdx.x, gridDim.x);
-      Seg sx = {0, 0, 0, 0};
-      const uint64_t pol_x = l2_policy_evict_last();
-      // 1: loaded, 0: slot still busy (non-blocking attempt), -1: no such k-block or abort
-      auto load_x = [&](int jj, bool block) -> int {
-        const int xs = jj % XSTAGES;
-        const uint32_t par = ((jj / XSTAGES) & 1) ^ 1;
-        if (jj >= XSTAGES) {
-          if (block) {
-            if (!mbar_wait(&xempty[xs], par, abort_flag, kSitePProd)) return -1;
-          } else if (!mbar_try_wait(&xempty[xs], par)) {
-            return 0;
-          }
-        }
-        while (!xseg || jj >= xbase + sx.nkb) {
-          if (xseg) xbase += sx.nkb;
-          xseg = wx.next(sc, sx);
-          if (!xseg) return -1;
-        }
-        const int kx = (sx.k0 + (jj - xbase)) * C::BK, m0 = (sx.t % sc.m_tiles) * BM;
-        mbar_arrive_expect_tx(&xfull[xs], C::X_BYTES);
-        tma_load_2d(sX + xs * C::X_BYTES, &tm_x, &xfull[xs], kx, m0, pol_x);
-        tma_load_2d(sX + xs * C::X_BYTES + C::X_PANEL, &tm_x, &xfull[xs], kx + 64, m0, pol_x);
-        return 1;
-      };
-      if constexpr (C::ISSUER_X) pdl_wait();  // activations may come from the preceding kernel
       for (; ok && wk.next(sc, sg); ++j) {
         const int b = j % DBUF;
         if (!mbar_wait(&dempty[b], ((j / DBUF) & 1) ^ 1, abort_flag, kSitePMmaD)) break;
@@ -557,12 +520,6 @@ __global__ void __launch_bounds__(512, 1)
         uint32_t acc = 0;  // 0 until this issuer's first MMA of the segment
         for (int i = 0; i < sg.nkb; ++i, ++it) {
           if (NI > 1 && it % NI != h) continue;
-          if constexpr (C::ISSUER_X) {
-            for (; ok && jx <= it; jx += NI) ok = load_x(jx, true) > 0;  // this k-block's tile, at least
-            for (; ok && jx <= it + XSTAGES - NI; jx += NI)               // and ahead while slots are free
-              if (load_x(jx, false) <= 0) break;
-            if (!ok) break;
-          }
           const int s = it % XSTAGES;
           const uint32_t ph = (it / XSTAGES) & 1;
           const int t = it % ASTAGES;
@@ -571,7 +528,6 @@ __global__ void __launch_bounds__(512, 1)
             ok = false;
             break;
           }
-          xcons = it + NI;
           tc_fence_after();
           const uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
 #pragma unroll
@@ -584,12 +540,6 @@ __global__ void __launch_bounds__(512, 1)
           umma_commit(&aempty[t]);
         }
         if (ok) umma_commit(&dfull[b]);
-      }
-      if constexpr (C::ISSUER_X) {
-        // activation tiles this issuer loaded and never waited for (after an abort) land before the
-        // CTA may exit (the look-ahead loads nothing past the CTA's last k-block)
-        for (int jj = xcons; jj < jx; jj += NI)
-          mbar_wait(&xfull[jj % XSTAGES], (jj / XSTAGES) & 1, nullptr, kSitePDrain);
       }
       // every issued MMA has completed before TMEM is released
       umma_commit(final_bar);
