@@ -827,31 +827,34 @@ __global__ void lora_simt_kernel(const __half* __restrict__ A, const __half* __r
 // Reference-order delta / merge on the CUDA cores (the `exact` entry points): every output is the
 // reference kernels' own j-ordered fp32 accumulation, acc = fmaf(B[n,j], A[j,k], acc) for
 // j = 0 .. r-1, rounded as they round it (lora_ops.cu:16-27, :32-38), so delta, the merged weight
-// and its requantisation equal the reference pipeline bit for bit.  A thread computes 4 rows x 4
-// columns; the block's 16 rows of B sit in shared memory as fp32, A is read 4 columns at a time.
-constexpr int kExactRows = 16;
-constexpr int kExactMaxR = 1024;  // 64 KB of B rows in shared memory
+// and its requantisation equal the reference pipeline bit for bit.  A thread computes 8 rows x 4
+// columns; the block's 32 rows of B sit in shared memory as fp32, transposed ([j][row], a padded
+// row of 36 so a thread's 8 values of one j are two 16-byte reads shared by its warp), and A is
+// read 4 columns at a time.
+constexpr int kExactRows = 32;
+constexpr int kExactLd = kExactRows + 4;  // padded [j] stride of the transposed B rows
+constexpr int kExactMaxR = 1024;          // 144 KB of B in shared memory
 
 template <int MODE, bool VEC>
 __global__ void __launch_bounds__(128) lora_exact_kernel(const __half* __restrict__ A, const __half* __restrict__ B,
                                                          const __half* W, int64_t ldw, __half* out, int64_t ldo, int N,
                                                          int K, int r, float s) {
-  extern __shared__ float sB[];  // [kExactRows][r]
+  extern __shared__ float4 sB4[];  // [r][kExactLd / 4]
+  float* sB = reinterpret_cast<float*>(sB4);
   const int n0 = blockIdx.y * kExactRows;
   for (int i = threadIdx.x; i < kExactRows * r; i += blockDim.x) {
-    const int rr = i / r;
-    sB[i] = n0 + rr < N ? __half2float(B[static_cast<int64_t>(n0 + rr) * r + (i - rr * r)]) : 0.f;
+    const int j = i / kExactRows, rr = i - j * kExactRows;
+    sB[j * kExactLd + rr] = n0 + rr < N ? __half2float(B[static_cast<int64_t>(n0 + rr) * r + j]) : 0.f;
   }
   __syncthreads();
-  const int cg = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int cg = threadIdx.x & 31, rg = threadIdx.x >> 5;  // rows rg*8 .. rg*8+7 of the block
   const int k0 = blockIdx.x * 128 + cg * 4;
   if (k0 >= K) return;
-  float acc[4][4];
+  float acc[8][4];
 #pragma unroll
-  for (int rr = 0; rr < 4; ++rr)
+  for (int rr = 0; rr < 8; ++rr)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[rr][e] = 0.f;
-  const float* brow = sB + rg * 4 * r;
   for (int j = 0; j < r; ++j) {
     float a[4];
     const __half* ap = A + static_cast<int64_t>(j) * K + k0;
@@ -865,16 +868,16 @@ __global__ void __launch_bounds__(128) lora_exact_kernel(const __half* __restric
 #pragma unroll
       for (int e = 0; e < 4; ++e) a[e] = k0 + e < K ? __half2float(ap[e]) : 0.f;
     }
+    const float4 b0 = sB4[(j * kExactLd + rg * 8) / 4], b1 = sB4[(j * kExactLd + rg * 8) / 4 + 1];
+    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-    for (int rr = 0; rr < 4; ++rr) {
-      const float b = brow[rr * r + j];
+    for (int rr = 0; rr < 8; ++rr)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[rr][e] = fmaf(b, a[e], acc[rr][e]);
-    }
+      for (int e = 0; e < 4; ++e) acc[rr][e] = fmaf(b[rr], a[e], acc[rr][e]);
   }
 #pragma unroll
-  for (int rr = 0; rr < 4; ++rr) {
-    const int n = n0 + rg * 4 + rr;
+  for (int rr = 0; rr < 8; ++rr) {
+    const int n = n0 + rg * 8 + rr;
     if (n >= N) break;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -1176,7 +1179,7 @@ static int launch_lora_exact(int mode, const void* a, const void* b, const void*
     return check_launch("lora_simt_kernel");
   }
   const dim3 grid(static_cast<unsigned>((k + 127) / 128), static_cast<unsigned>((n + kExactRows - 1) / kExactRows));
-  const size_t smem = static_cast<size_t>(kExactRows) * r * sizeof(float);
+  const size_t smem = static_cast<size_t>(kExactLd) * r * sizeof(float);
   const bool vec = k % 4 == 0 && reinterpret_cast<uintptr_t>(a) % 8 == 0;
   const __half* A = static_cast<const __half*>(a);
   const __half* B = static_cast<const __half*>(b);
@@ -1186,7 +1189,7 @@ static int launch_lora_exact(int mode, const void* a, const void* b, const void*
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [] {
-    const int bytes = kExactRows * kExactMaxR * sizeof(float);
+    const int bytes = kExactLd * kExactMaxR * sizeof(float);
     cudaFuncSetAttribute(lora_exact_kernel<kModeDelta, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(lora_exact_kernel<kModeDelta, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(lora_exact_kernel<kModeMerge, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
