@@ -14,10 +14,13 @@ without finishing its output.  This module turns that into Python errors:
 * ``set_wait_limit(seconds)`` / ``wait_limit()`` set and read the bound of every
   spin wait on a device (default 4 s).
 * ``Trace`` records, per CTA of each traced kernel launch, globaltimer stamps of
-  its phases (start, first weight tile landed, last MMA complete, epilogue
-  done, the deferred stream-K reductions done, and for the fused all-gather:
-  call epoch read, every peer's outputs received; and when the preceding
-  kernel completed), so a caller can see which phase bounds a step.
+  its phases, so a caller can see which phase bounds a step.  The W8A16 GEMM:
+  start, first weight tile landed, last MMA complete, epilogue done, the
+  deferred stream-K reductions done, and for the fused all-gather: call epoch
+  read, every peer's outputs received; and when the preceding kernel completed.
+  The fused merge + requantisation: start, first accumulator of each pass
+  ready, pass 1 done (grid-barrier arrival), grid barrier passed, pass 2 done,
+  and when its TMA producer and MMA issuer finished each pass.
 """
 from __future__ import annotations
 
@@ -88,8 +91,13 @@ def wait_limit(device=None) -> float:
 
 PHASES = ("start", "first_tile", "mma_done", "epilogue_done", "reduce_done", "epoch_read", "gather_done",
           "predecessor_done")
+# the fused merge + requantisation kernel's phases: its two passes over the items, the grid
+# barrier between them, and when its TMA producer and first MMA issuer finished each pass
+REQUANT_PHASES = ("start", "first_item", "pass1_done", "barrier_passed", "pass2_first_item", "pass2_done",
+                  "pass1_loads_issued", "loads_issued", "mma_pass1_done", "mma_done")
 RECORD_WORDS = 16
-KERNEL_IDS = {1: "w8a16_persistent", 2: "w8a16_persistent_swiglu"}
+KERNEL_IDS = {1: "w8a16_persistent", 2: "w8a16_persistent_swiglu", 3: "lora_requant_coop"}
+KERNEL_PHASES = {3: REQUANT_PHASES}
 
 
 @dataclass
@@ -97,8 +105,9 @@ class Launch:
     grid_id: int
     kernel: str
     ctas: int
-    stamps: torch.Tensor  # [ctas, len(PHASES)] int64 ns, 0 = not reached
+    stamps: torch.Tensor  # [ctas, len(phases)] int64 ns, 0 = not reached
     smid: torch.Tensor    # [ctas] SM of each CTA
+    phases: tuple = PHASES
 
     def phases_us(self) -> dict:
         """Phase ends relative to the first CTA start, in microseconds (max over CTAs), and
@@ -106,7 +115,7 @@ class Launch:
         s = self.stamps.double()
         t0 = float(s[:, 0][s[:, 0] > 0].min())
         out = {"cta_start_spread": round((float(s[:, 0].max()) - t0) / 1e3, 3)}
-        for i, name in enumerate(PHASES[1:], start=1):
+        for i, name in enumerate(self.phases[1:], start=1):
             col = s[:, i][s[:, i] > 0]
             if col.numel():
                 out[name] = round((float(col.max()) - t0) / 1e3, 3)
@@ -153,7 +162,8 @@ class Trace:
             ctas = int(rows[0, 1]) >> 32
             order = torch.argsort(rows[:, 1] & 0xFFFFFFFF)
             kid = int(rows[0, 2]) & 0xFFFFFFFF
-            out.append(Launch(gid, KERNEL_IDS.get(kid, str(kid)), ctas, rows[order, 3:3 + len(PHASES)],
-                              (rows[order, 2] >> 32) & 0xFFFFFFFF))
+            names = KERNEL_PHASES.get(kid, PHASES)
+            out.append(Launch(gid, KERNEL_IDS.get(kid, str(kid)), ctas, rows[order, 3:3 + len(names)],
+                              (rows[order, 2] >> 32) & 0xFFFFFFFF, names))
         out.sort(key=lambda l: int(l.stamps[:, 0][l.stamps[:, 0] > 0].min()))
         return out

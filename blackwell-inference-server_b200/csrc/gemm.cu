@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(512, 1)
                             const __grid_constant__ CUtensorMap tm_x, const void* __restrict__ scale_in,
                             const void* __restrict__ scale2, int sdtype, void* __restrict__ y_in, int64_t ldy_in,
                             int M, int N_in, const Sched sc, float* __restrict__ ws, int* __restrict__ counters,
-                            const GatherArgs g, const __grid_constant__ GroupArgs grp) {
+                            const __grid_constant__ GatherArgs g, const __grid_constant__ GroupArgs grp) {
   using C = PCfg<BM>;
   constexpr int STAGES = C::STAGES;
   constexpr int XSTAGES = C::XSTAGES;
@@ -996,7 +996,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const int w = w0 + i * 2 * C::THREADS;
-                if (w >= rows * 64) break;
+                if (!ok || w >= rows * 64) continue;  // no break: the loop stays unrolled, v in registers
                 const uint64_t* a = src + static_cast<size_t>(w >> 6) * g.rowwords + (w & 63);
                 while (static_cast<uint32_t>(v[i][0] >> 32) != ep || static_cast<uint32_t>(v[i][1] >> 32) != ep) {
                   if (clock64() - tw0 > limit) {
@@ -1007,7 +1007,7 @@ __global__ void __launch_bounds__(512, 1)
                   }
                   ld_ll2(a, v[i][0], v[i][1]);
                 }
-                if (!ok) break;
+                if (!ok) continue;
                 // 4 outputs: token w / 64, columns 2 (w % 64) .. + 3 of the tile
                 const int c = 2 * (w & 63);
                 uint16_t* d = dst + static_cast<int64_t>(w >> 6) * ldy_in + c;

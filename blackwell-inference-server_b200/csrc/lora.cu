@@ -453,6 +453,9 @@ __device__ __forceinline__ unsigned req_max_bits(__half2 hm) {
 }
 
 static_assert(512 + kReqMaxProblems * sizeof(ReqProblem) <= kReqBarBytes, "problem table does not fit");
+// mbarriers (B full/empty, accumulator full/empty, ring full/empty, final), then 24 bytes of slots
+// (TMEM address, abort flag, barrier generation, trace record)
+static_assert((4 + 2 * kReqSlots + 2 * kReqMaxStages + 2) * 8 + 24 <= 512, "barrier area");
 
 __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const __grid_constant__ ReqBatch batch) {
   extern __shared__ uint8_t smem_raw[];
@@ -479,6 +482,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_gen = abort_flag + 1;  // barrier generation seen at entry
+  unsigned long long** trace_slot = reinterpret_cast<unsigned long long**>(tmem_slot + 4);
   ReqProblem* sp = reinterpret_cast<ReqProblem*>(smem + batch.off_bar + 512);  // problem table
 
   const int warp = threadIdx.x >> 5;
@@ -506,6 +510,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
     mbar_init(&final_bar[1], 1);
     *abort_flag = 0;
     *s_gen = ld_acquire_gpu(&gsync[1]);  // before this CTA arrives: the same value in every CTA
+    *trace_slot = trace_claim(3);
     fence_mbar_init();
   }
   if (warp == 0 && lane < count) {
@@ -523,6 +528,12 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // phase stamps: 0 start, 1 first accumulator ready, 2 pass 1 done (grid-barrier arrival),
+  // 3 grid barrier passed, 4 first pass-2 accumulator ready, 5 last code block stored,
+  // 6 / 7 the TMA producer has issued every pass-1 / every load, 8 / 9 MMA issuer 0 reached
+  // pass 2 / its MMAs completed
+  unsigned long long* const trec = *trace_slot;
+  if (threadIdx.x == 0) trace_stamp(trec, 0);
 
   // B buffer use: a new buffer whenever (problem, row block) changes along the walk
   // or pass 2 starts; the walk repeats identically in pass 2.
@@ -538,6 +549,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         if (it == nmine) {
           w = req_walk_at(sp, count, lo);
           prev_pi = -1;  // pass 2 starts with a fresh B buffer
+          trace_stamp(trec, 6);
         }
         const int pi = w.pi, rb = w.rb, panel = w.panel;
         const int nbp = sp[pi].nbp;
@@ -561,6 +573,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         tma_load_2d(slot + 16384, &batch.tm_a[pi], &full[st], panel * 64, 0, keep);
         req_walk_next(w, sp, count);
       }
+      trace_stamp(trec, 7);
     }
   } else if (warp == 1 || warp == kReqMmaWarp2) {
     // ---------------- MMA issuers: items alternate between the two ----------------
@@ -578,6 +591,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         if (it == nmine) {
           w = req_walk_at(sp, count, lo);
           prev_pi = -1;
+          if (me == 0) trace_stamp(trec, 8);
         }
         const int pi = w.pi, rb = w.rb;
         const int rp = sp[pi].rp;
@@ -611,6 +625,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
       }
       umma_commit(&final_bar[me]);  // every issued MMA has completed before TMEM is freed
       mbar_wait(&final_bar[me], 0, nullptr, kSiteReqFinal);
+      if (me == 0) trace_stamp(trec, 9);
     }
   } else {
     // ---------------- epilogue: warps 2 .. 2 + 4*kReqGroups - 1 ----------------
@@ -639,6 +654,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         // only the spinning thread knows the outcome: it alone votes, the OR spreads it
         bool grid_failed = false;
         if (ew == 0 && lane == 0) {
+          trace_stamp(trec, 2);
           // self-resetting barrier: the last arrival clears the count and opens the next generation
           if (atomicAdd(&gsync[0], 1) == G - 1) {
             __threadfence();
@@ -659,6 +675,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
         }
         if (named_bar_any(1, kReqEpiThreads, grid_failed)) bad = true;
         __threadfence();
+        if (ew == 0 && lane == 0) trace_stamp(trec, 3);
       }
       int cur_pi = -1, cur_rb = -1, cur_row = -1;
       __half2 hm = __float2half2_rn(0.0f);
@@ -703,6 +720,7 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
           bad = true;
           break;
         }
+        if ((ew & 3) == 0 && lane == 0 && it == it0) trace_stamp(trec, 1 + 3 * pass);  // the pass's first item
         tc_fence_after();
         const uint8_t* wrow = sRing + st * stage_bytes + row * 128;
         if (pass == 1) {
@@ -771,6 +789,8 @@ __global__ void __launch_bounds__(kReqThreads, 1) lora_requant_coop_kernel(const
       if (pass == 0 && !bad && cur_row >= 0) atomicMax(&rowmax[2 * cur_row + set], req_max_bits(hm));
     }
     if (lane == 0) tma_store_wait0();
+    named_bar_sync(1, kReqEpiThreads);
+    if (ew == 0 && lane == 0) trace_stamp(trec, 5);
   }
 
   tc_fence_before();
