@@ -90,38 +90,30 @@ __device__ __forceinline__ int8_t quant_fast(float w, float s, float rcp) {
 // is rounded to fp16 in packed form, clamped to +-127 and rounded to an
 // integer by adding 1536 (fp16 spacing is exactly 1 on [1024, 2048), so the
 // addition is round-to-nearest-even, and the half's low byte is the code).
-// Lanes whose x is within 4 fp32 ulps of an fp16 rounding midpoint redo that
-// element with the exact IEEE division.
-// Flagged lanes of quant4_f16: redo the elements whose quotient is near a
-// midpoint with the exact division.  Out of line: it runs for a few elements in
-// ten thousand, and inlining it sixteen times per row would crowd the
-// instruction cache of the hot loop.
-static __device__ __noinline__ uint32_t quant4_fix(uint32_t packed, __half2 w01, __half2 w23, float s, float rcp) {
-  const float2 f01 = __half22float2(w01);
-  const float2 f23 = __half22float2(w23);
-  const float f[4] = {f01.x, f01.y, f23.x, f23.y};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    if (((__float_as_uint(__fmul_rn(f[e], rcp)) + 4u) & 0x1FF8u) == 0x1000u) {
-      const uint32_t code = static_cast<uint8_t>(quant_one<BW_DTYPE_F16>(f[e], s));
-      packed = (packed & ~(0xFFu << (8 * e))) | (code << (8 * e));
-    }
-  }
-  return packed;
-}
-
+//
+// No lane needs the exact division.  x differs from RN32(w / s) by at most a few
+// fp32 ulps, so the two could only round to different fp16 values if w / s lay
+// at or next to an fp16 rounding midpoint m.  It is never at one: w = m * s
+// would make w's odd significand (at most 11 bits) a multiple of m's (12 bits,
+// odd).  That it is never close enough to one is not argued but enumerated: for
+// every finite fp16 w and every positive finite fp16 s (2.0e9 pairs, subnormal
+// scales included) this packed path gives quant_one's code
+// (tests/quant_fast_check.cpp, f16packed and f16packed_noclamp at stride 1).
+// A midpoint check with an out-of-line fix-up cost the fused merge +
+// requantisation kernel 16 % of its time.
+//
 // CLAMP = false is for rows whose scale is a normal fp16 number (>= 2^-14):
 // then every |w| <= the row maximum gives |x| < 127.07, fp16(x) stays within
 // +-127.0625 and the rounding lands on codes -127..127 without the clamp.
 template <bool CLAMP = true>
 __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s, float rcp) {
+  (void)s;
   // packed fp32 multiplies: each lane is the IEEE round-to-nearest product
   const float2 x01 = __fmul2_rn(__half22float2(w01), make_float2(rcp, rcp));
   const float2 x23 = __fmul2_rn(__half22float2(w23), make_float2(rcp, rcp));
-  const float x[4] = {x01.x, x01.y, x23.x, x23.y};
   const __half2 bias = __float2half2_rn(1536.0f);
-  __half2 y01 = __floats2half2_rn(x[0], x[1]);
-  __half2 y23 = __floats2half2_rn(x[2], x[3]);
+  __half2 y01 = __float22half2_rn(x01);
+  __half2 y23 = __float22half2_rn(x23);
   if constexpr (CLAMP) {
     const __half2 lim = __float2half2_rn(127.0f);
     const __half2 nlim = __float2half2_rn(-127.0f);
@@ -133,10 +125,6 @@ __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s
   uint32_t packed;
   asm("prmt.b32 %0, %1, %2, 0x6420;" : "=r"(packed) : "r"(*reinterpret_cast<uint32_t*>(&y01)),
       "r"(*reinterpret_cast<uint32_t*>(&y23)));
-  bool near = false;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) near |= ((__float_as_uint(x[e]) + 4u) & 0x1FF8u) == 0x1000u;
-  if (near) packed = quant4_fix(packed, w01, w23, s, rcp);
   return packed;
 }
 
@@ -144,23 +132,11 @@ __device__ __forceinline__ uint32_t quant4_f16(__half2 w01, __half2 w23, float s
 // has a finite reciprocal: x = RN32(w * rcp) rounded to bf16 in packed form,
 // clamped to +-127 in bf16, rounded to an integer by adding 1.5 * 2^23 in fp32
 // (spacing 1 there, so the add is round-to-nearest-even) and the code is the low
-// byte of the sum.  x within 4 fp32 ulps (low 16 bits) of a bf16 rounding
-// midpoint takes the exact division.  Checked against quant_one<bf16> for every
-// finite bf16 weight and every such scale.
-static __device__ __noinline__ uint32_t quant4_bf16_fix(uint32_t packed, __nv_bfloat162 w01, __nv_bfloat162 w23,
-                                                        float s, float rcp) {
-  const float f[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    if (((__float_as_uint(__fmul_rn(f[e], rcp)) + 4u) & 0xFFF8u) == 0x8000u) {
-      const uint32_t code = static_cast<uint8_t>(quant_one<BW_DTYPE_BF16>(f[e], s));
-      packed = (packed & ~(0xFFu << (8 * e))) | (code << (8 * e));
-    }
-  }
-  return packed;
-}
-
+// byte of the sum.  As for fp16, no lane needs the exact division: enumerated
+// for every finite bf16 weight and every such scale (1.9e9 pairs,
+// tests/quant_fast_check.cpp bf16packed at stride 1).
 __device__ __forceinline__ uint32_t quant4_bf16(__nv_bfloat162 w01, __nv_bfloat162 w23, float s, float rcp) {
+  (void)s;
   const float2 x01 = __fmul2_rn(__bfloat1622float2(w01), make_float2(rcp, rcp));
   const float2 x23 = __fmul2_rn(__bfloat1622float2(w23), make_float2(rcp, rcp));
   const __nv_bfloat162 lim = __float2bfloat162_rn(127.0f);
@@ -174,11 +150,6 @@ __device__ __forceinline__ uint32_t quant4_bf16(__nv_bfloat162 w01, __nv_bfloat1
   asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(t01) : "r"(__float_as_uint(z01.x)), "r"(__float_as_uint(z01.y)));
   asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(t23) : "r"(__float_as_uint(z23.x)), "r"(__float_as_uint(z23.y)));
   asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(packed) : "r"(t01), "r"(t23));
-  const bool near = ((((__float_as_uint(x01.x) + 4u) & 0xFFF8u) == 0x8000u) |
-                     (((__float_as_uint(x01.y) + 4u) & 0xFFF8u) == 0x8000u) |
-                     (((__float_as_uint(x23.x) + 4u) & 0xFFF8u) == 0x8000u) |
-                     (((__float_as_uint(x23.y) + 4u) & 0xFFF8u) == 0x8000u));
-  if (near) packed = quant4_bf16_fix(packed, w01, w23, s, rcp);
   return packed;
 }
 

@@ -4,7 +4,8 @@
 // For every finite weight w and every positive finite scale s of the dtype,
 // the fast path (x = RN32(w * RN32(1/s)), exact division only when x is within
 // 4 fp32 ulps of a rounding midpoint, non-finite, or (fp32) near an integer +
-// 1/2) must give the same int8 code as the exact path
+// 1/2; the packed fp16 and bf16 paths have no such fix-up at all) must give the
+// same int8 code as the exact path
 // (clamp(rint(dt(RN32(w / s))), -127, 127), NaN -> 0).  x86-64 SSE float
 // arithmetic is IEEE single precision; build without fast-math or FP
 // contraction.
@@ -70,14 +71,13 @@ template <int DT> static int8_t quant_fast(float w, float s, float rcp, long* sl
 
 // Emulation of quant4_f16 (csrc/quant_math.cuh) for one element: packed fp16
 // rounding, fp16 clamp to +-127, +1536 in fp16 (round-to-nearest-even to an
-// integer), code = low byte of the half; exact path when x is near an fp16
-// rounding midpoint.  Valid for finite, non-zero scales.
+// integer), code = low byte of the half.  No exact-division fix-up: the kernel
+// has none, and the sweep shows that none is needed.  Valid for finite, non-zero
+// scales.
 static int8_t quant_packed_f16(float w, float s, float rcp, long* slow_count) {
+  (void)s;
+  (void)slow_count;
   volatile float x = w * rcp;
-  if (((f_to_bits(x) + 4u) & 0x1FF8u) == 0x1000u) {
-    ++*slow_count;
-    return quant_exact<F16>(w, s);
-  }
   _Float16 y = static_cast<_Float16>(x);
   if (y > static_cast<_Float16>(127.0f)) y = static_cast<_Float16>(127.0f);
   if (y < static_cast<_Float16>(-127.0f)) y = static_cast<_Float16>(-127.0f);
@@ -90,13 +90,12 @@ static int8_t quant_packed_f16(float w, float s, float rcp, long* slow_count) {
 
 // quant4_f16 without the +-127 clamp, used for rows whose scale is a normal
 // fp16 number: every |w| <= amax of the row gives |x| < 127.07, so fp16(x)
-// stays within +-127.0625 and the +1536 rounding lands on 1409..1663.
+// stays within +-127.0625 and the +1536 rounding lands on 1409..1663.  No
+// midpoint check and no exact-division fix-up, as in the kernel.
 static int8_t quant_packed_f16_noclamp(float w, float s, float rcp, long* slow_count) {
+  (void)s;
+  (void)slow_count;
   volatile float x = w * rcp;
-  if (((f_to_bits(x) + 4u) & 0x1FF8u) == 0x1000u) {
-    ++*slow_count;
-    return quant_exact<F16>(w, s);
-  }
   const _Float16 y = static_cast<_Float16>(x);
   volatile _Float16 z = static_cast<_Float16>(static_cast<float>(y) + 1536.0f);
   uint16_t bits;
@@ -149,14 +148,12 @@ static void run_packed_noclamp(int stride) {
 // Emulation of quant4_bf16 (csrc/quant_math.cuh) for one element: x = RN32(w*rcp)
 // rounded to bf16, clamped to +-127 in bf16, rounded to an integer by adding
 // 1.5*2^23 in fp32 (spacing 1 there: round-to-nearest-even), code = low byte of
-// the sum's bits; exact path when x's low 16 bits are within 4 of 0x8000 (a bf16
-// rounding midpoint).  Valid for finite, non-zero scales.
+// the sum's bits.  No exact-division fix-up, as in the kernel.  Valid for
+// finite, non-zero scales.
 static int8_t quant_packed_bf16(float w, float s, float rcp, long* slow_count) {
+  (void)s;
+  (void)slow_count;
   volatile float x = w * rcp;
-  if (((f_to_bits(x) + 4u) & 0xFFF8u) == 0x8000u) {
-    ++*slow_count;
-    return quant_exact<BF16>(w, s);
-  }
   float y = round_bf16(x);
   if (y > 127.0f) y = 127.0f;
   if (y < -127.0f) y = -127.0f;
