@@ -432,9 +432,10 @@ struct ReqCodes {
 };
 
 // Codes of a row whose scale is not a normal fp16 number: subnormal (packed
-// quantiser with its clamp) or zero / inf / NaN (closed form).  Out of line:
-// such rows are rare and the hot loop stays small.
-static __device__ __noinline__ ReqCodes req_codes_rare(ReqHalfRow m, float scale, float rcp, bool fast_row) {
+// quantiser with its clamp) or zero / inf / NaN (closed form).  Inline: as an
+// out-of-line call it took a 64-byte argument through the stack and left the
+// kernel with register spills (cfg2 2.6 % slower); inline, the kernel has none.
+static __device__ __forceinline__ ReqCodes req_codes_rare(ReqHalfRow m, float scale, float rcp, bool fast_row) {
   ReqCodes q;
   if (fast_row) {
 #pragma unroll
