@@ -317,13 +317,19 @@ int bw_get_wait_limit_ns(uint64_t* ns);
 /*
  * Device-side phase trace for the current device (no reference counterpart;
  * the reference profiles with torch.profiler).  While a buffer is set, each
- * CTA of a traced kernel (the W8A16 GEMM family) claims one 128-byte record
+ * CTA of a traced kernel claims one 128-byte record
  *   u64 {gridid, blockIdx | gridDim << 32, kernel id | smid << 32, t[0..12]}
- * with globaltimer stamps (ns; 0 = phase not reached): t0 CTA start, t1 first
- * weight tile in shared memory, t2 last MMA complete, t3 epilogue done, and
- * for the all-gather variant t4 this CTA's stores fenced and counted, t5 the
- * peers' ready flags seen, t6 the completion handshake done (the CTA that ran
- * it), t7 the preceding kernel complete (griddepcontrol.wait returned).
+ * with globaltimer stamps (ns; 0 = phase not reached).
+ * Kernel ids 1 and 2, the W8A16 GEMM and its SwiGLU variant: t0 CTA start,
+ * t1 first weight tile in shared memory, t2 last MMA complete, t3 epilogue
+ * done, t4 the deferred stream-K reductions done, and for the all-gather
+ * variant t5 the call's epoch read, t6 every peer's outputs received; t7 the
+ * preceding kernel complete (griddepcontrol.wait returned).
+ * Kernel id 3, the fused merge + requantisation: t0 CTA start, t1 / t4 the
+ * first accumulator of pass 1 / pass 2 ready, t2 pass 1 done (grid-barrier
+ * arrival), t3 grid barrier passed, t5 the last codes stored, t6 / t7 the TMA
+ * producer has issued every pass-1 load / every load, t8 / t9 the first MMA
+ * issuer reached pass 2 / its MMAs completed.
  * buffer = NULL turns tracing off; bw_trace_records gives the records written
  * so far (records past the buffer's capacity are dropped).
  */
